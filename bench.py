@@ -1,0 +1,358 @@
+#!/usr/bin/env python3
+"""Batched-decode benchmark for the promptboot_b200 engine.
+
+Workload: the config-0 model (seeded synthetic Qwen2.5-0.5B Q4_0, PBTQW25 v1),
+`--seqs` independent sequences per GPU (default 256), each with a 512-token
+uniform random prompt (numpy default_rng(0x5eed0000 + global_index)) and its
+own SamplingState(global_index), decoding with the interactive sampler
+(penalty 1.1 over the whole history, T 0.7, top-k 20, top-p 0.8).  One step =
+one sampled token for every sequence: sampler + 24-layer forward + lm_head +
+greedy argmax, all device resident.  Prefill (512 lockstep forward steps) and
+`--warmup` steps are untimed; exactly `--steps` steps are timed with CUDA
+events on the engine's stream between barriers + synchronizes, max over ranks.
+Sequences are partitioned by rank (weak scaling: `--seqs` per GPU) and share no
+data, so the hot path has no collective.
+
+`--impl reference` times the reference's decode arithmetic on the host cores
+instead (the CPU restatement in oracle/, since the reference's Rust cannot be
+built here), one sequence per host thread, same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decoded tok/s, Qwen2.5-0.5B Q4_0 batch 256 at 1/2/4/8 B200; % HBM roofline"
+UNIT = "tok/s"
+PROMPT_SEED = 0x5EED0000
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=32)
+    p.add_argument("--warmup", type=int, default=4)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--seqs", type=int, default=256, help="sequences per GPU")
+    p.add_argument("--prompt", type=int, default=512)
+    p.add_argument("--context", type=int, default=1536)
+    p.add_argument("--e2e-steps", type=int, default=8)
+    p.add_argument("--cpu-tokens", type=int, default=6, help="CPU-baseline tokens per thread")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def model_image(rank: int, world: int):
+    from promptboot_b200 import pbtqw25
+    if rank == 0:
+        img = pbtqw25.load_or_synthesize(0)
+    barrier(world)
+    if rank != 0:
+        img = pbtqw25.load_or_synthesize(0)
+    return img
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.path = pathlib.Path(tempfile.mkstemp(prefix="pb_clocks_", suffix=".csv")[1])
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in self.path.read_text().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                if len(f) >= 9 and f[1].isdigit():
+                    rows.append(f)
+        except OSError:
+            pass
+        finally:
+            self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(int(r[1]) for r in rows),
+                "sm_max_mhz": max(int(r[2]) for r in rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops_sustained", 1400.0), "measured"
+    return 6650.0, 1400.0, "fallback"
+
+
+def profiled_traffic(kernel_class: str):
+    """DRAM bytes per launch from the committed ncu summary, if one covers the class."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if kernel_class in d:
+            return d[kernel_class]
+    return None
+
+
+KC = {"embed": 0, "norm": 1, "gemv": 2, "rope_kv": 3, "attention": 4, "quant": 5, "swiglu": 6,
+      "lm_head": 7, "argmax": 8, "sampler": 9}
+
+
+def algorithmic_bytes(cls: str, seqs: int, start_pos: int, steps: int) -> float:
+    """Algorithmic bytes of all launches of `cls` over `steps` steps whose first
+    step evaluates position start_pos for every sequence."""
+    mean_ctx = start_pos + (steps - 1) / 2.0 + 1.0
+    if cls == "attention":
+        # per layer: (positions) x (K 512 B + V 512 B) + q in + out (896 f32 each)
+        return steps * 24 * seqs * (mean_ctx * 1024.0 + 2 * 896 * 4)
+    if cls == "gemv":
+        mats = [(896, 896), (128, 896), (128, 896), (896, 896), (4864, 896), (4864, 896), (896, 4864)]
+        per_layer = sum(r * k // 32 * 18 + seqs * (k * 4 + r * 4) for r, k in mats)
+        return steps * 24 * per_layer
+    if cls == "lm_head":
+        return steps * (151936 * 28 * 34 + seqs * (896 * 4 + 151936 * 4))
+    if cls == "sampler":
+        return steps * seqs * (151936 * 4 + mean_ctx * 4)
+    return 0.0
+
+
+def cpu_baseline(img, threads: int, tokens: int, start: int):
+    import oracle
+    oracle.bench_decode(img, start, 1, threads, threads)  # page in weights
+    t0 = time.perf_counter()
+    oracle.bench_decode(img, start, tokens, threads, threads)
+    dt = time.perf_counter() - t0
+    return threads * tokens / dt, dt
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    import oracle
+    from promptboot_b200 import pbtqw25
+    img = pbtqw25.load_or_synthesize(0)
+    cores = oracle.cpu_cores()
+    oracle.bench_decode(img, args.prompt, max(args.warmup, 1), cores, cores)
+    t0 = time.perf_counter()
+    oracle.bench_decode(img, args.prompt, args.steps, cores, cores)
+    dt = time.perf_counter() - t0
+    value = cores * args.steps / dt
+    sample = (f"{cores} sequences (one per host thread) x {args.steps} decode tokens from "
+              f"context {args.prompt}, oracle/ C restatement (-O3 -mavx2)")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt * 1000.0 / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4->f32/f64",
+            "data": "synthetic (seeded random-init weights, uniform random prompts)",
+            "config": {"workload": "config 3 batched decode (CPU sample)", "seqs": cores,
+                       "context_start": args.prompt},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    import ctypes
+    import torch
+    from promptboot_b200 import _lib, api
+    torch.cuda.set_device(local)
+    img = model_image(rank, world)
+    S, P, C = args.seqs, args.prompt, args.context
+    if P + args.warmup + args.steps + args.e2e_steps + 1 > C:
+        C = ((P + args.warmup + args.steps + args.e2e_steps + 4) + 3) // 4 * 4
+    model = api.ModelView(img, device=local)
+    eng = api.InferenceEngine(model, max_seqs=S, max_context=C)
+    lib = _lib.load()
+    seqs = np.arange(S, dtype=np.uint32)
+    gidx = rank * S + np.arange(S)
+    prompts = np.stack([np.random.default_rng(PROMPT_SEED + int(g)).integers(0, 151643, P, dtype=np.uint32)
+                        for g in gidx])
+    status, _, errs = eng.prefill_batch(seqs, prompts, C - P)
+    if status:
+        raise RuntimeError(f"prefill failed: {errs[0].tuple()}")
+    states = [api.SamplingState(int(g)) for g in gidx]
+    stream = torch.cuda.ExternalStream(lib.pb_engine_stream(eng._h))
+
+    # warm-up with every kernel class timed, to name the dominant kernel
+    lib.pb_engine_profile(eng._h, 0xFFFF)
+    st, _, errs = eng.generate(seqs, states, args.warmup, want_tokens=False)
+    if st:
+        raise RuntimeError(f"warm-up failed: {[e.tuple() for e in errs if e.status][:1]}")
+    ms = (ctypes.c_double * 16)()
+    cnt = (ctypes.c_uint64 * 16)()
+    lib.pb_engine_profile_read(eng._h, ms, cnt)
+    by_class = {name: ms[i] for name, i in KC.items()}
+    dominant = max(by_class, key=by_class.get)
+    lib.pb_engine_profile(eng._h, 1 << KC[dominant])
+
+    start_pos = P + args.warmup
+    launches0 = lib.pb_engine_launch_count(eng._h)
+    clock = ClockSampler(local)
+    with clock:
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        st, _, errs = eng.generate(seqs, states, args.steps, want_tokens=False)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    if st:
+        raise RuntimeError(f"timed steps failed: {[e.tuple() for e in errs if e.status][:1]}")
+    elapsed_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    launches = lib.pb_engine_launch_count(eng._h) - launches0
+    lib.pb_engine_profile_read(eng._h, ms, cnt)
+    dom_ms, dom_n = ms[KC[dominant]], cnt[KC[dominant]]
+    lib.pb_engine_profile(eng._h, 0)
+
+    # end to end through the C ABI with host buffers: decode_batch + sample per step
+    e2e_steps = args.e2e_steps
+    tokens = np.zeros(S, dtype=np.uint32)
+    st, ids, _ = eng.sample(seqs, states)
+    tokens[:] = ids
+    barrier(world)
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(e2e_steps):
+        st, steps, errs = eng.decode_batch(seqs, tokens, require_greedy=False)
+        st2, ids, _ = eng.sample(seqs, states)
+        tokens[:] = ids
+    a1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(a0.elapsed_time(a1), world)
+
+    total_tokens = S * world * args.steps
+    value = total_tokens / (elapsed_ms / 1000.0)
+    e2e_value = S * world * e2e_steps / (e2e_ms / 1000.0)
+    hbm, tflops_sus, peak_kind = measured_peaks()
+    alg = algorithmic_bytes(dominant, S, start_pos, args.steps)
+    achieved = (alg / (dom_ms / 1000.0)) / 1e9 if dom_ms > 0 else None
+    traffic = profiled_traffic(dominant)
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            import oracle
+            cores = oracle.cpu_cores()
+            v, dt = cpu_baseline(img, cores, args.cpu_tokens, P)
+            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                   "sample": f"{cores} sequences x {args.cpu_tokens} decode tokens from context {P} "
+                             f"on {cores} host threads ({dt:.1f} s), oracle/ C restatement"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8xint4->f32/f64", "data": "synthetic (seeded random-init weights, uniform random prompts)",
+            "config": {"workload": "config 3 batched decode", "seqs_per_gpu": S,
+                       "global_batch": S * world, "prompt": P, "context_capacity": C,
+                       "timed_positions": [start_pos, start_pos + args.steps - 1],
+                       "parallelism": f"sequence-partitioned x{world}, no collective",
+                       "l2": "inputs larger than L2 (346 MB weights + KV per step)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "steps": e2e_steps,
+                    "h2d_bytes_per_step": 36 * S, "d2h_bytes_per_step": 48 * S},
+            "gpu_launches": int(launches),
+            "roofline": {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": hbm,
+                         "unit": "GB/s", "frac": (achieved / hbm) if achieved else None,
+                         "traffic": traffic, "peak_source": peak_kind,
+                         "launches": int(dom_n), "avg_launch_us": 1000.0 * dom_ms / max(dom_n, 1),
+                         "warmup_ms_by_class": {k: round(v, 3) for k, v in by_class.items()}},
+            "clocks": clock.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    model.close()
+    return line
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

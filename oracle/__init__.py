@@ -84,6 +84,7 @@ def lib():
             "orc_generate": (u32, [P, P, sz, P, P, u32, u32, ctypes.c_uint64, ctypes.c_int,
                                    P, P, P, P]),
             "orc_generate_many": (u32, [P, sz, P, u32, P, u32, u32, P, u32, P]),
+            "orc_bench_decode": (u32, [P, sz, P, u32, u32, u32, P, u32, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -271,3 +272,14 @@ def cpu_cores() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover
         return os.cpu_count() or 1
+
+
+def bench_decode(model: np.ndarray, start_position: int, steps: int, nseq: int, threads: int,
+                 seeds=None) -> None:
+    """CPU baseline work: nseq sequences x `steps` decode tokens from start_position."""
+    seeds = np.ascontiguousarray(np.arange(nseq) if seeds is None else seeds, dtype=np.uint64)
+    cap = ((start_position + steps + 3) // 4) * 4
+    st = lib().orc_bench_decode(_p(model), cap, _p(rope_table()), start_position, steps, nseq,
+                                _p(seeds), threads, None)
+    if st:
+        raise RuntimeError(f"oracle bench failed with status {st}")

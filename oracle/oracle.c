@@ -658,3 +658,78 @@ uint32_t orc_generate_many(const uint8_t *file, size_t capacity, const float *ro
     pthread_mutex_destroy(&pool.lock);
     return pool.status;
 }
+
+/* CPU baseline of one batched-decode step per sequence (the reference's per-token
+ * work: inference.rs:1454-1765 forward + inference.rs:919-965 sampler) from a
+ * context of start_position tokens.  The KV below start_position is filled with
+ * seeded values: the decode arithmetic's cost does not depend on them. */
+typedef struct {
+    const uint8_t *file;
+    size_t capacity;
+    const float *rope;
+    uint32_t start, steps, nseq;
+    const uint64_t *seeds;
+    uint32_t *out_tokens;
+    uint32_t next;
+    pthread_mutex_t lock;
+} orc_bench;
+
+static void *bench_worker(void *arg) {
+    orc_bench *b = (orc_bench *)arg;
+    size_t kv_words = 24 * 2 * 2 * b->capacity * 64;
+    float *kv = (float *)malloc(kv_words * sizeof(float));
+    float *logits = (float *)malloc(151936 * sizeof(float));
+    uint32_t *history = (uint32_t *)malloc(((size_t)b->start + b->steps + 1) * 4);
+    uint8_t *seen = (uint8_t *)calloc(18992, 1);
+    orc_scratch *s = (orc_scratch *)calloc(1, sizeof *s);
+    s->scores = (float *)calloc(b->capacity + 4, sizeof(float));
+    for (;;) {
+        pthread_mutex_lock(&b->lock);
+        uint32_t seq = b->next++;
+        pthread_mutex_unlock(&b->lock);
+        if (seq >= b->nseq) break;
+        uint64_t lcg = b->seeds[seq] * 6364136223846793005ull + 1442695040888963407ull;
+        for (size_t i = 0; i < kv_words; ++i) {
+            lcg = lcg * 6364136223846793005ull + 1442695040888963407ull;
+            kv[i] = (float)((int32_t)(lcg >> 40) - (1 << 23)) * (1.0f / 8388608.0f);
+        }
+        for (uint32_t i = 0; i < b->start; ++i) {
+            lcg = lcg * 6364136223846793005ull + 1442695040888963407ull;
+            history[i] = (uint32_t)((lcg >> 33) % 151643u);
+        }
+        uint64_t state = b->seeds[seq] == 0 ? 0x9e3779b97f4a7c15ull : b->seeds[seq], draws = 0;
+        uint32_t token = history[b->start - 1];
+        orc_error err;
+        for (uint32_t t = 0; t < b->steps; ++t) {
+            uint32_t pos = b->start + t;
+            history[pos] = token;
+            if (forward_scratch(b->file, kv, b->capacity, b->rope, token, pos, logits, &err, s)) break;
+            uint32_t sel = 0;
+            if (orc_sample_with_repetition(logits, 151936, history, pos + 1, seen, 18992, &state,
+                                           &draws, &sel, &err))
+                break;
+            if (b->out_tokens) b->out_tokens[(size_t)seq * b->steps + t] = sel;
+            token = sel;
+        }
+    }
+    free(s->scores); free(s); free(seen); free(history); free(logits); free(kv);
+    return NULL;
+}
+
+uint32_t orc_bench_decode(const uint8_t *file, size_t capacity, const float *rope,
+                          uint32_t start_position, uint32_t steps, uint32_t nseq,
+                          const uint64_t *seeds, uint32_t threads, uint32_t *out_tokens) {
+    if (start_position == 0 || start_position + steps > capacity) return 2;
+    orc_bench b;
+    memset(&b, 0, sizeof b);
+    b.file = file; b.capacity = capacity; b.rope = rope; b.start = start_position;
+    b.steps = steps; b.nseq = nseq; b.seeds = seeds; b.out_tokens = out_tokens;
+    pthread_mutex_init(&b.lock, NULL);
+    if (threads < 1) threads = 1;
+    pthread_t *tid = (pthread_t *)malloc(threads * sizeof(pthread_t));
+    for (uint32_t t = 0; t < threads; ++t) pthread_create(&tid[t], NULL, bench_worker, &b);
+    for (uint32_t t = 0; t < threads; ++t) pthread_join(tid[t], NULL);
+    free(tid);
+    pthread_mutex_destroy(&b.lock);
+    return 0;
+}

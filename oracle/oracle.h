@@ -93,6 +93,12 @@ uint32_t orc_generate_many(const uint8_t *file, size_t capacity, const float *ro
                            uint32_t decode_steps, const uint64_t *seeds, uint32_t threads,
                            uint32_t *out_tokens);
 
+/* CPU baseline: nseq independent sequences on worker threads, each decoding
+ * `steps` tokens (forward + sampler) from start_position over a seeded KV */
+uint32_t orc_bench_decode(const uint8_t *file, size_t capacity, const float *rope,
+                          uint32_t start_position, uint32_t steps, uint32_t nseq,
+                          const uint64_t *seeds, uint32_t threads, uint32_t *out_tokens);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,438 @@
+// Decode-step kernels for sm_100a: embedding, RMSNorm + Q8_0 quantizer, the
+// Q4_0 / Q8_0 block-scaled matrix-vector products, RoPE + KV write, GQA decode
+// attention, SwiGLU + quantizer and the greedy argmax.
+//
+// Each kernel follows the operation order of the reference's scalar code
+// (sulewicz/promptboot crates/promptboot-core/src/fp32_sse2.rs), cited per
+// kernel, so that its binary32 results are the reference's bit for bit.
+#include "pb_common.cuh"
+#include "pb_kernels.cuh"
+
+#include <cstdio>
+
+namespace pb {
+
+// ---------------------------------------------------------------- reductions
+
+__device__ __forceinline__ double warp_sum_f64(double v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max_f32(float v) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int warp_sum_i32(int v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ------------------------------------------------------------------ embedding
+
+// fp32_sse2.rs:897-922: hidden = fl(d * (q - 8)), low nibbles are elements 0-15.
+// The token is also recorded in the slot's history (the sampler's penalty set).
+__global__ void embed_kernel(Batch b, const uint8_t* __restrict__ emb) {
+  int row = blockIdx.x;
+  uint32_t token = b.tokens[row];
+  const uint8_t* w = emb + (size_t)token * 28 * 18;
+  for (int e = threadIdx.x; e < kHidden; e += blockDim.x) {
+    const uint8_t* block = w + (e >> 5) * 18;
+    float d = half_to_f32((uint16_t)(block[0] | (block[1] << 8)));
+    int i = e & 31;
+    uint8_t packed = block[2 + (i & 15)];
+    int q = (i < 16 ? (packed & 0x0f) : (packed >> 4)) - 8;
+    float h = __fmul_rn(d, __int2float_rn(q));
+    b.hidden[(size_t)row * kHidden + e] = h;
+    check_finite(h, &b.err[row], 0, D_EMBEDDING, 0, e);
+  }
+  if (threadIdx.x == 0)
+    b.history[(size_t)b.slots[row] * b.capacity + b.positions[row]] = token;
+}
+
+void launch_embed(const Batch& b, const uint8_t* embedding, cudaStream_t s) {
+  embed_kernel<<<b.rows, 128, 0, s>>>(b, embedding);
+}
+
+// ------------------------------------------------------------ Q8_0 quantizer
+
+// fp32_sse2.rs:945-983, one warp per 32-element block: d = amax / 127 rounded to
+// binary16 for storage, inverse from the unrounded d, q = trunc(x * inv +- 0.5).
+// The block's quant sum is kept for the Q4_0 zero-point correction.
+__device__ __forceinline__ void quantize_block_warp(float x, int8_t* aq, float* ad, int* asum) {
+  float amax = warp_max_f32(fbits(bitsf(x) & 0x7fffffffu));
+  float d = __fdiv_rn(amax, 127.0f);
+  float inverse = bitsf(d) == 0 ? 0.0f : __fdiv_rn(1.0f, d);
+  float v = __fmul_rn(x, inverse);
+  float half = (bitsf(v) >> 31) == 0 ? 0.5f : -0.5f;
+  int q = __float2int_rz(__fadd_rn(v, half));
+  int lane = threadIdx.x & 31;
+  aq[lane] = (int8_t)q;
+  int total = warp_sum_i32((int)(int8_t)q);
+  if (lane == 0) {
+    *ad = half_to_f32(f32_to_half(bitsf(d)));
+    *asum = total;
+  }
+}
+
+// fp32_sse2.rs:1310-1334 then the quantizer.  The f64 sum of squares is reduced
+// across the block instead of in index order: the terms are binary32 squares
+// whose f64 sum is exact whenever their exponents lie within 29 binades of the
+// largest, and otherwise differs only far below the binary32 rounding of the
+// mean, so the f32 result matches the reference's serial sum.
+__global__ void rmsnorm_quant_kernel(Batch b, const float* __restrict__ weight,
+                                     uint32_t layer_ordinal, uint32_t domain) {
+  __shared__ float y[kHidden];
+  __shared__ double partial[8];
+  int row = blockIdx.x;
+  const float* x = b.hidden + (size_t)row * kHidden;
+  double sum = 0.0;
+  for (int e = threadIdx.x; e < kHidden; e += blockDim.x) {
+    float v = x[e];
+    sum += (double)__fmul_rn(v, v);
+  }
+  sum = warp_sum_f64(sum);
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) partial[warp] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += partial[w];
+    partial[0] = t;
+  }
+  __syncthreads();
+  float mean = (float)(partial[0] / 896.0);
+  float inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, fbits(0x358637bdu))));
+  for (int e = threadIdx.x; e < kHidden; e += blockDim.x) {
+    float v = __fmul_rn(__fmul_rn(x[e], inverse), weight[e]);
+    y[e] = v;
+    if (b.norm_out) b.norm_out[(size_t)row * kHidden + e] = v;
+    check_finite(v, &b.err[row], layer_ordinal, domain, 0, e);
+  }
+  __syncthreads();
+  for (int blk = warp; blk < kHidden / 32; blk += blockDim.x >> 5) {
+    quantize_block_warp(y[blk * 32 + lane], b.aq + (size_t)row * kActStride + blk * 32,
+                        b.ad + (size_t)row * kActBlocks + blk,
+                        b.asum + (size_t)row * kActBlocks + blk);
+  }
+}
+
+void launch_rmsnorm_quant(const Batch& b, const float* weight, uint32_t layer_ordinal,
+                          uint32_t domain, cudaStream_t s) {
+  rmsnorm_quant_kernel<<<b.rows, 256, 0, s>>>(b, weight, layer_ordinal, domain);
+}
+
+__global__ void quant_kernel(Batch b, const float* __restrict__ x, size_t ld, int columns) {
+  int row = blockIdx.x;
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int blk = warp; blk < columns / 32; blk += blockDim.x >> 5) {
+    quantize_block_warp(x[(size_t)row * ld + blk * 32 + lane],
+                        b.aq + (size_t)row * kActStride + blk * 32,
+                        b.ad + (size_t)row * kActBlocks + blk,
+                        b.asum + (size_t)row * kActBlocks + blk);
+  }
+}
+
+void launch_quant(const Batch& b, const float* x, size_t ld, int columns, cudaStream_t s) {
+  quant_kernel<<<b.rows, 256, 0, s>>>(b, x, ld, columns);
+}
+
+// fp32_sse2.rs:1751-1770 then the quantizer: product = fl(fl(g / (1 + e)) * u)
+// with e = expf4(0 - g); checked as the SWIGLU stage.
+__global__ void swiglu_quant_kernel(Batch b, uint32_t layer_ordinal) {
+  int row = blockIdx.x;
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* g = b.gate + (size_t)row * kFfn;
+  const float* u = b.up + (size_t)row * kFfn;
+  for (int blk = warp; blk < kFfn / 32; blk += blockDim.x >> 5) {
+    int e = blk * 32 + lane;
+    float gv = g[e];
+    float ex = expf4_lane(__fsub_rn(0.0f, gv));
+    float silu = __fdiv_rn(gv, __fadd_rn(1.0f, ex));
+    float p = __fmul_rn(silu, u[e]);
+    if (b.product_out) b.product_out[(size_t)row * kFfn + e] = p;
+    check_finite(p, &b.err[row], layer_ordinal, D_SWIGLU, 0, e);
+    quantize_block_warp(p, b.aq + (size_t)row * kActStride + blk * 32,
+                        b.ad + (size_t)row * kActBlocks + blk,
+                        b.asum + (size_t)row * kActBlocks + blk);
+  }
+}
+
+void launch_swiglu_quant(const Batch& b, uint32_t layer_ordinal, cudaStream_t s) {
+  swiglu_quant_kernel<<<b.rows, 256, 0, s>>>(b, layer_ordinal);
+}
+
+// ------------------------------------------------ block-scaled matvec (GEMV)
+//
+// y[b][r] = sum over blocks k, IN ORDER, in binary32 of
+//   Q4_0: fl(fl(f32(i32dot) * dW) * dA)   (fp32_sse2.rs:1217-1248)
+//   Q8_0: fl(f32(i32dot) * fl(dW * dA))   (fp32_sse2.rs:1250-1281)
+// The exact int32 block dots and the per-block terms are computed in parallel
+// (phase 1, terms staged in shared memory); the order-sensitive binary32 sum
+// runs per (row, sequence) in block order (phase 2).  Q4_0 nibbles enter dp4a
+// unsigned (0..15) and the zero point is removed exactly as -8 * sum(a).
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvSeqChunk = 8;
+
+__device__ __forceinline__ uint32_t ld_u32_2aligned(const uint8_t* p) {
+  // p is 2-byte aligned in shared memory
+  uint32_t lo = *reinterpret_cast<const uint16_t*>(p);
+  uint32_t hi = *reinterpret_cast<const uint16_t*>(p + 2);
+  return lo | (hi << 16);
+}
+
+template <int BPB, int RT>
+__global__ void __launch_bounds__(kGemvThreads)
+qgemv_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilogue ep) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int tid = threadIdx.x;
+  const int r0 = blockIdx.x * RT;
+  const size_t row_bytes = (size_t)nb * BPB;
+  const int wbytes = RT * nb * BPB;
+  const int wbytes_padded = (wbytes + 15) & ~15;
+  const int tstride = nb + 1;
+  uint8_t* wt = smem;
+  float* terms = reinterpret_cast<float*>(smem + wbytes_padded);
+
+  const uint4* src = reinterpret_cast<const uint4*>(w + (size_t)r0 * row_bytes);
+  for (int i = tid; i < wbytes / 16; i += kGemvThreads) reinterpret_cast<uint4*>(wt)[i] = src[i];
+  __syncthreads();
+
+  for (int s0 = 0; s0 < b.rows; s0 += kGemvSeqChunk) {
+    const int sb = min(kGemvSeqChunk, b.rows - s0);
+    for (int item = tid; item < RT * nb; item += kGemvThreads) {
+      const int r = item / nb, blk = item - r * nb;
+      const uint8_t* bp = wt + (size_t)(r * nb + blk) * BPB;
+      const float dW = half_to_f32(*reinterpret_cast<const uint16_t*>(bp));
+      uint32_t wq[8];
+      if (BPB == 18) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t p = ld_u32_2aligned(bp + 2 + 4 * j);
+          wq[j] = p & 0x0f0f0f0fu;
+          wq[4 + j] = (p >> 4) & 0x0f0f0f0fu;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wq[j] = ld_u32_2aligned(bp + 2 + 4 * j);
+      }
+      for (int s = 0; s < sb; ++s) {
+        const int row = s0 + s;
+        const uint4* ap = reinterpret_cast<const uint4*>(b.aq + (size_t)row * kActStride + blk * 32);
+        const uint4 a0 = ap[0], a1 = ap[1];
+        const int aw[8] = {(int)a0.x, (int)a0.y, (int)a0.z, (int)a0.w,
+                           (int)a1.x, (int)a1.y, (int)a1.z, (int)a1.w};
+        int dot = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dot = __dp4a((int)wq[j], aw[j], dot);
+        const float dA = b.ad[(size_t)row * kActBlocks + blk];
+        float term;
+        if (BPB == 18) {
+          dot -= 8 * b.asum[(size_t)row * kActBlocks + blk];
+          term = __fmul_rn(__fmul_rn(__int2float_rn(dot), dW), dA);
+        } else {
+          term = __fmul_rn(__int2float_rn(dot), __fmul_rn(dW, dA));
+        }
+        terms[(s * RT + r) * tstride + blk] = term;
+      }
+    }
+    __syncthreads();
+    for (int item = tid; item < sb * RT; item += kGemvThreads) {
+      const int s = item / RT, r = item - s * RT;
+      const float* t = terms + (s * RT + r) * tstride;
+      float acc = 0.0f;
+      for (int blk = 0; blk < nb; ++blk) acc = __fadd_rn(acc, t[blk]);
+      const int row = s0 + s, orow = r0 + r;
+      float* dst = ep.out + (size_t)row * ep.ld + orow;
+      float v;
+      if (ep.mode == EPI_BIAS) v = __fadd_rn(acc, ep.bias[orow]);
+      else if (ep.mode == EPI_RESIDUAL) v = __fadd_rn(*dst, acc);
+      else v = acc;
+      *dst = v;
+      check_finite(v, &ep.err[row], ep.layer_ordinal, ep.domain, 0, orow);
+    }
+    __syncthreads();
+  }
+}
+
+template <int BPB, int RT>
+static size_t qgemv_smem(int nb) {
+  int wbytes = RT * nb * BPB;
+  return (size_t)((wbytes + 15) & ~15) + (size_t)kGemvSeqChunk * RT * (nb + 1) * 4;
+}
+
+void launch_qgemv(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
+                  const Epilogue& ep, cudaStream_t s) {
+  const int nb = columns / 32;
+  if (wtype == W_Q4_0) {
+    if (nb > 64) {
+      constexpr int RT = 8;
+      qgemv_kernel<18, RT><<<rows / RT, kGemvThreads, qgemv_smem<18, RT>(nb), s>>>(w, rows, nb, b, ep);
+    } else {
+      constexpr int RT = 32;
+      qgemv_kernel<18, RT><<<rows / RT, kGemvThreads, qgemv_smem<18, RT>(nb), s>>>(w, rows, nb, b, ep);
+    }
+  } else {
+    if (nb > 64) {
+      constexpr int RT = 8;
+      qgemv_kernel<34, RT><<<rows / RT, kGemvThreads, qgemv_smem<34, RT>(nb), s>>>(w, rows, nb, b, ep);
+    } else {
+      constexpr int RT = 32;
+      qgemv_kernel<34, RT><<<rows / RT, kGemvThreads, qgemv_smem<34, RT>(nb), s>>>(w, rows, nb, b, ep);
+    }
+  }
+}
+
+// ------------------------------------------------------------- RoPE and KV
+
+// fp32_sse2.rs:1413-1428 on q (14 heads) and k (2 heads), then the KV write of
+// inference.rs:1809-1887 (tiled K, row-major V).  Checks: ROPE q, ROPE k, KV k.
+__global__ void rope_kv_kernel(Batch b, int layer, const float* __restrict__ rope) {
+  int row = blockIdx.x;
+  int position = b.positions[row];
+  uint32_t ord = (uint32_t)layer + 1;
+  const float* table = rope + (size_t)position * 64;
+  float* q = b.q + (size_t)row * kHidden;
+  float* k = b.k + (size_t)row * 128;
+  const float* v = b.v + (size_t)row * 128;
+  float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * b.capacity * 64;
+  for (int item = threadIdx.x; item < 16 * 32; item += blockDim.x) {
+    int head = item >> 5, pair = item & 31;
+    float* x = head < 14 ? q + head * 64 : k + (head - 14) * 64;
+    float left = x[pair], right = x[pair + 32];
+    float c = table[pair * 2], sn = table[pair * 2 + 1];
+    float l2 = __fsub_rn(__fmul_rn(left, c), __fmul_rn(right, sn));
+    float r2 = __fadd_rn(__fmul_rn(left, sn), __fmul_rn(right, c));
+    x[pair] = l2;
+    x[pair + 32] = r2;
+    if (head < 14) {
+      check_finite(l2, &b.err[row], ord, D_ROPE, 0, head * 64 + pair);
+      check_finite(r2, &b.err[row], ord, D_ROPE, 0, head * 64 + pair + 32);
+    } else {
+      int kh = head - 14;
+      check_finite(l2, &b.err[row], ord, D_ROPE, 1, kh * 64 + pair);
+      check_finite(r2, &b.err[row], ord, D_ROPE, 1, kh * 64 + pair + 32);
+      check_finite(l2, &b.err[row], ord, D_KV, 0, kh * 64 + pair);
+      check_finite(r2, &b.err[row], ord, D_KV, 0, kh * 64 + pair + 32);
+      kv[kv_key_word(b.capacity, layer, kh, position, pair)] = l2;
+      kv[kv_key_word(b.capacity, layer, kh, position, pair + 32)] = r2;
+    }
+  }
+  for (int i = threadIdx.x; i < 128; i += blockDim.x)
+    kv[kv_value_word(b.capacity, layer, i >> 6, position, i & 63)] = v[i];
+}
+
+void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s) {
+  rope_kv_kernel<<<b.rows, 256, 0, s>>>(b, layer, rope);
+}
+
+// --------------------------------------------------------------- attention
+//
+// fp32_sse2.rs:1430-1672 for one (sequence, query head) per CTA:
+//   score_p = fl(f32(sum_c f64(fl(q_c * k_pc))) * 0.125)   (c in order, one thread per p)
+//   max over p; span padded to a multiple of 4 with -inf
+//   e = expf4(s - max); sum += f64(fl(fl(e0+e1) + fl(e2+e3))) over 4-groups in order
+//   p = fl(e * f32(1.0 / sum));  out_c = f32(sum_p f64(fl(p * v_pc)))  (p in order)
+// Every order-sensitive f64 sum is sequential as in the reference.
+
+__global__ void attention_kernel(Batch b, int layer) {
+  __shared__ float qs[64];
+  __shared__ float red[8];
+  __shared__ double total;
+  const int row = blockIdx.x / kQHeads, qh = blockIdx.x % kQHeads, kh = qh / 7;
+  const int positions = b.positions[row] + 1;
+  const int span = max((positions + 3) & ~3, b.span_min);
+  const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * b.capacity * 64;
+  float* sc = b.scores + ((size_t)row * kQHeads + qh) * b.score_stride;
+  if (threadIdx.x < 64) qs[threadIdx.x] = b.q[(size_t)row * kHidden + qh * 64 + threadIdx.x];
+  __syncthreads();
+  float local_max = fbits(0xff800000u);
+  for (int p = threadIdx.x; p < positions; p += blockDim.x) {
+    double dot = 0.0;
+    for (int c = 0; c < 64; ++c)
+      dot += (double)__fmul_rn(qs[c], kv[kv_key_word(b.capacity, layer, kh, p, c)]);
+    float s = __fmul_rn((float)dot, 0.125f);
+    sc[p] = s;
+    if (s > local_max) local_max = s;
+  }
+  local_max = warp_max_f32(local_max);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = local_max;
+  __syncthreads();
+  float maximum = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) maximum = fmaxf(maximum, red[w]);
+  for (int p = positions + threadIdx.x; p < span; p += blockDim.x) sc[p] = fbits(0xff800000u);
+  __syncthreads();
+  for (int p = threadIdx.x; p < span; p += blockDim.x) sc[p] = expf4_lane(__fsub_rn(sc[p], maximum));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double sum = 0.0;
+    for (int p = 0; p < span; p += 4)
+      sum += (double)__fadd_rn(__fadd_rn(sc[p], sc[p + 1]), __fadd_rn(sc[p + 2], sc[p + 3]));
+    total = sum;
+  }
+  __syncthreads();
+  const float normalizer = (float)(1.0 / total);
+  for (int p = threadIdx.x; p < positions; p += blockDim.x) sc[p] = __fmul_rn(sc[p], normalizer);
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    const int c = threadIdx.x;
+    double acc = 0.0;
+    for (int p = 0; p < positions; ++p)
+      acc += (double)__fmul_rn(sc[p], kv[kv_value_word(b.capacity, layer, kh, p, c)]);
+    float o = (float)acc;
+    b.attn[(size_t)row * kHidden + qh * 64 + c] = o;
+    check_finite(o, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh * 64 + c);
+  }
+}
+
+void launch_attention(const Batch& b, int layer, cudaStream_t s) {
+  attention_kernel<<<b.rows * kQHeads, 256, 0, s>>>(b, layer);
+}
+
+// -------------------------------------------------------------- argmax/top8
+
+// fp32_sse2.rs:1772-1784: first maximum by strict > (lowest id among equal
+// values, +0 and -0 equal).  Also records the first non-finite word.
+__global__ void argmax_kernel(const float* __restrict__ logits, size_t ld, int words,
+                              uint32_t* ids, uint32_t* bits_out,
+                              unsigned long long* first_nonfinite) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const float* x = logits + (size_t)blockIdx.x * ld;
+  float best = fbits(0xff800000u);
+  int besti = 0x7fffffff;
+  for (int i = threadIdx.x; i < words; i += blockDim.x) {
+    float v = x[i];
+    uint32_t vb = bitsf(v);
+    if (!finite_bits(vb) && first_nonfinite)
+      atomicMin(&first_nonfinite[blockIdx.x], ((unsigned long long)i << 32) | vb);
+    if (v > best || besti == 0x7fffffff) { best = v; besti = i; }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+    if (ov > best || (!(best > ov) && oi < besti)) { best = ov; besti = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { bv[threadIdx.x >> 5] = best; bi[threadIdx.x >> 5] = besti; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (bv[w] > best || (!(best > bv[w]) && bi[w] < besti)) { best = bv[w]; besti = bi[w]; }
+    ids[blockIdx.x] = (uint32_t)besti;
+    if (bits_out) bits_out[blockIdx.x] = bitsf(x[besti]);
+  }
+}
+
+void launch_argmax(const float* logits, size_t ld, int rows, int words, uint32_t* ids,
+                   uint32_t* bits, unsigned long long* first_nonfinite, cudaStream_t s) {
+  argmax_kernel<<<rows, 1024, 0, s>>>(logits, ld, words, ids, bits, first_nonfinite);
+}
+
+void init_kernel_attributes() {
+  cudaFuncSetAttribute(qgemv_kernel<18, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaFuncSetAttribute(qgemv_kernel<18, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaFuncSetAttribute(qgemv_kernel<34, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaFuncSetAttribute(qgemv_kernel<34, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
+
+}  // namespace pb

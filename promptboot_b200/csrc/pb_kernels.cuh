@@ -1,0 +1,88 @@
+// Launch-side declarations of the decode kernels (implemented in pb_kernels.cu
+// and pb_sampler.cu).  Everything here is device pointers and sizes; the host
+// engine (pb_engine.cu) sequences these per token step.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace pb {
+
+// Per-row buffers of one forward batch; row b of every [B][...] array belongs to
+// engine slot slots[b], which owns KV region slots[b] and writes position
+// positions[b] this step.
+struct Batch {
+  int rows;                 // B
+  const int* slots;         // [B]
+  const int* positions;     // [B]
+  const uint32_t* tokens;   // [B] token evaluated this step
+  float* hidden;            // [B][896] residual stream
+  int8_t* aq;               // [B][4864] Q8_0 activation quants
+  float* ad;                // [B][152] activation scales (binary16 value as f32)
+  int* asum;                // [B][152] sum of the 32 quants of each block
+  float* q;                 // [B][896]
+  float* k;                 // [B][128]
+  float* v;                 // [B][128]
+  float* attn;              // [B][896]
+  float* gate;              // [B][4864]
+  float* up;                // [B][4864]
+  float* logits;            // [B][151936]
+  float* scores;            // [B][14][score_stride] attention scratch
+  size_t score_stride;
+  float* kv;                // slot-major KV cache
+  size_t capacity;          // positions per slot
+  uint32_t* history;        // [slots][capacity] tokens evaluated so far
+  unsigned long long* err;  // [B] ranked first stage failure
+  float* norm_out = nullptr;     // optional [B][896] RMSNorm output (operator API)
+  float* product_out = nullptr;  // optional [B][4864] SwiGLU output (operator API)
+  int span_min = 0;              // minimum softmax span (operator API; 0 = natural)
+};
+
+enum EpiMode : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
+
+struct Epilogue {
+  int mode;
+  float* out;             // output base (row b at out + b * ld)
+  size_t ld;
+  const float* bias;      // EPI_BIAS
+  unsigned long long* err;
+  uint32_t layer_ordinal;
+  uint32_t domain;
+};
+
+enum WeightType : int { W_Q4_0 = 2, W_Q8_0 = 3 };
+
+// Kernel launchers (stream-ordered, asynchronous).
+void launch_embed(const Batch& b, const uint8_t* embedding, cudaStream_t s);
+void launch_rmsnorm_quant(const Batch& b, const float* weight, uint32_t layer_ordinal,
+                          uint32_t domain, cudaStream_t s);
+void launch_quant(const Batch& b, const float* x, size_t ld, int columns, cudaStream_t s);
+void launch_qgemv(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
+                  const Epilogue& ep, cudaStream_t s);
+void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s);
+void launch_attention(const Batch& b, int layer, cudaStream_t s);
+void launch_swiglu_quant(const Batch& b, uint32_t layer_ordinal, cudaStream_t s);
+void launch_argmax(const float* logits, size_t ld, int rows, int words, uint32_t* ids,
+                   uint32_t* bits, unsigned long long* first_nonfinite, cudaStream_t s);
+void launch_topk8(const float* logits, size_t ld, int rows, int words, uint32_t* out_pairs,
+                  unsigned long long* first_nonfinite, cudaStream_t s);
+
+// Sampler: rows of logits mutated in place by the repetition penalty, then one
+// draw per row from states[row]; out[row] = selected id.  status[row] != 0 marks
+// a rejected row (nothing mutated, no draw); detail[row] carries the reference's
+// error fields (see pb_sampler.cu).
+struct SamplerRow {
+  uint32_t status;       // 0 ok, 3 TOKEN_ID, 7 NONFINITE_OUTPUT
+  uint32_t index;        // offending logit index or history position
+  uint32_t value;        // offending bits or token id
+  uint32_t selected;
+};
+void launch_sampler(float* logits, size_t ld, int rows, int words, const uint32_t* history,
+                    const uint64_t* hist_offset, const uint32_t* hist_len,
+                    const uint8_t* initial_seen, unsigned long long* states, SamplerRow* out,
+                    cudaStream_t s);
+
+void init_kernel_attributes();
+
+}  // namespace pb

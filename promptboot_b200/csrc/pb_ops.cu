@@ -1,0 +1,329 @@
+// Host-buffer sampler entry points (inference.rs:814-965 of sulewicz/promptboot)
+// and the device-pointer kernel operators of the C ABI.
+#include "pb_common.cuh"
+#include "pb_host.h"
+#include "pb_kernels.cuh"
+
+#include <algorithm>
+#include <vector>
+
+namespace {
+
+constexpr uint32_t NO_LAYER = 0xffffffffu;
+constexpr uint32_t NO_TENSOR = 0xffffffffu;
+constexpr uint64_t kV = 151936;
+
+void set_err(pb_error* e, uint32_t status, uint32_t domain, uint64_t needed, uint64_t available,
+             uint32_t kind, uint32_t sub) {
+  if (!e) return;
+  e->status = status; e->domain = domain; e->layer = NO_LAYER; e->position = 0;
+  e->tensor_id = NO_TENSOR; e->reserved = 0; e->needed = needed; e->available = available;
+  e->detail = ((uint64_t)kind << 32) | sub;
+}
+
+// inference.rs:737-753 (length) then inference.rs:883-903 (first non-finite word)
+uint32_t validate_logits(const uint32_t* logits, uint64_t len, pb_error* err) {
+  if (len != kV) { set_err(err, PB_CAPACITY, 18, kV, len, 12, 0); return PB_CAPACITY; }
+  for (uint64_t i = 0; i < len; ++i)
+    if ((logits[i] & 0x7f800000u) == 0x7f800000u) {
+      set_err(err, PB_NONFINITE_OUTPUT, 19, 0, logits[i], 7, (uint32_t)i);
+      return PB_NONFINITE_OUTPUT;
+    }
+  return PB_OK;
+}
+
+// Device buffers for the single-row host-API sampler calls.
+struct RowScratch {
+  float* logits = nullptr;
+  uint32_t* history = nullptr;
+  uint64_t* offset = nullptr;
+  uint32_t* length = nullptr;
+  uint8_t* seen = nullptr;
+  unsigned long long* state = nullptr;
+  pb::SamplerRow* out = nullptr;
+  uint32_t* pairs = nullptr;
+  uint32_t* ids = nullptr;
+  ~RowScratch() {
+    void* p[] = {logits, history, offset, length, seen, state, out, pairs, ids};
+    for (void* x : p) if (x) cudaFree(x);
+  }
+};
+
+uint32_t run_sampler_row(uint32_t* logits, const uint32_t* tokens, uint64_t count,
+                         const uint8_t* seen, pb_sampling_state* state, pb::SamplerRow* row,
+                         bool write_back) {
+  RowScratch s;
+  PB_CUDA(cudaMalloc(&s.logits, kV * 4));
+  PB_CUDA(cudaMalloc(&s.history, std::max<uint64_t>(count, 1) * 4));
+  PB_CUDA(cudaMalloc(&s.offset, 8));
+  PB_CUDA(cudaMalloc(&s.length, 4));
+  PB_CUDA(cudaMalloc(&s.state, 16));
+  PB_CUDA(cudaMalloc(&s.out, sizeof(pb::SamplerRow)));
+  if (seen) PB_CUDA(cudaMalloc(&s.seen, PB_SEEN_BYTES));
+  const uint64_t zero = 0;
+  const uint32_t n = (uint32_t)count;
+  PB_CUDA(cudaMemcpy(s.logits, logits, kV * 4, cudaMemcpyHostToDevice));
+  if (count) PB_CUDA(cudaMemcpy(s.history, tokens, count * 4, cudaMemcpyHostToDevice));
+  PB_CUDA(cudaMemcpy(s.offset, &zero, 8, cudaMemcpyHostToDevice));
+  PB_CUDA(cudaMemcpy(s.length, &n, 4, cudaMemcpyHostToDevice));
+  PB_CUDA(cudaMemcpy(s.state, state, 16, cudaMemcpyHostToDevice));
+  if (seen) PB_CUDA(cudaMemcpy(s.seen, seen, PB_SEEN_BYTES, cudaMemcpyHostToDevice));
+  pb::launch_sampler(s.logits, kV, 1, (int)kV, s.history, s.offset, s.length, s.seen, s.state,
+                     s.out, nullptr);
+  PB_CUDA(cudaGetLastError());
+  PB_CUDA(cudaMemcpy(row, s.out, sizeof(pb::SamplerRow), cudaMemcpyDeviceToHost));
+  if (row->status == 0) {
+    PB_CUDA(cudaMemcpy(state, s.state, 16, cudaMemcpyDeviceToHost));
+    if (write_back) PB_CUDA(cudaMemcpy(logits, s.logits, kV * 4, cudaMemcpyDeviceToHost));
+  }
+  return PB_OK;
+}
+
+__global__ void staging_kernel(const int8_t* aq, const float* ad, int rows, int blocks,
+                               uint8_t* staging) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * blocks) return;
+  int r = i / blocks, b = i % blocks;
+  uint8_t* out = staging + (size_t)i * 34;
+  uint16_t h = pb::f32_to_half(__float_as_uint(ad[(size_t)r * pb::kActBlocks + b]));
+  out[0] = (uint8_t)(h & 0xff);
+  out[1] = (uint8_t)(h >> 8);
+  for (int e = 0; e < 32; ++e) out[2 + e] = (uint8_t)aq[(size_t)r * pb::kActStride + b * 32 + e];
+}
+
+__global__ void iota_kernel(int* p, int n) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = i;
+}
+
+// Operator scratch: quantized activations, stage-error words, slot/position maps.
+struct OpScratch {
+  int8_t* aq = nullptr;
+  float* ad = nullptr;
+  int* asum = nullptr;
+  unsigned long long* err = nullptr;
+  int* slots = nullptr;
+  int* positions = nullptr;
+  cudaStream_t s;
+  explicit OpScratch(cudaStream_t st) : s(st) {}
+  cudaError_t alloc(uint32_t rows) {
+    cudaError_t e = cudaMallocAsync(&aq, (size_t)rows * pb::kActStride, s);
+    if (!e) e = cudaMallocAsync(&ad, (size_t)rows * pb::kActBlocks * 4, s);
+    if (!e) e = cudaMallocAsync(&asum, (size_t)rows * pb::kActBlocks * 4, s);
+    if (!e) e = cudaMallocAsync(&err, (size_t)rows * 8, s);
+    if (!e) e = cudaMallocAsync(&slots, (size_t)rows * 4, s);
+    if (!e) e = cudaMallocAsync(&positions, (size_t)rows * 4, s);
+    if (!e) e = cudaMemsetAsync(err, 0xff, (size_t)rows * 8, s);
+    if (!e) iota_kernel<<<(rows + 127) / 128, 128, 0, s>>>(slots, (int)rows);
+    return e;
+  }
+  ~OpScratch() {
+    void* p[] = {aq, ad, asum, err, slots, positions};
+    for (void* x : p) if (x) cudaFreeAsync(x, s);
+  }
+  pb::Batch batch(uint32_t rows) const {
+    pb::Batch b{};
+    b.rows = (int)rows; b.slots = slots; b.positions = positions; b.tokens = nullptr;
+    b.aq = aq; b.ad = ad; b.asum = asum; b.err = err;
+    return b;
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+void pb_sampling_state_init(pb_sampling_state* state, uint64_t seed) {
+  if (!state) return;
+  state->state = seed == 0 ? 0x9e3779b97f4a7c15ull : seed;
+  state->draws = 0;
+}
+
+uint32_t pb_sample_token(const uint32_t* logits, uint64_t len, pb_sampling_state* state,
+                         uint32_t* out, pb_error* err) {
+  uint32_t st = validate_logits(logits, len, err);
+  if (st) return st;
+  std::vector<uint32_t> copy(logits, logits + len);
+  pb::SamplerRow row{};
+  st = run_sampler_row(copy.data(), nullptr, 0, nullptr, state, &row, false);
+  if (st) return st;
+  if (out) *out = row.selected;
+  return PB_OK;
+}
+
+uint32_t pb_sample_token_with_repetition(uint32_t* logits, uint64_t len, const uint32_t* tokens,
+                                         uint64_t count, uint8_t* seen, uint64_t seen_len,
+                                         pb_sampling_state* state, uint32_t* out, pb_error* err) {
+  uint32_t st = validate_logits(logits, len, err);
+  if (st) return st;
+  const uint64_t need = (len + 7) / 8;
+  if (!seen || seen_len < need) {
+    set_err(err, PB_CAPACITY, 19, need, seen ? seen_len : 0, 4, 2);
+    return PB_CAPACITY;
+  }
+  for (uint64_t i = 0; i < count; ++i)
+    if (tokens[i] >= len) {
+      set_err(err, PB_TOKEN_ID, 19, len, tokens[i], 2, 0);
+      return PB_TOKEN_ID;
+    }
+  pb::SamplerRow row{};
+  st = run_sampler_row(logits, tokens, count, seen, state, &row, true);
+  if (st) return st;
+  // fp32_sse2.rs:1871-1875: every history token's bit is cleared afterwards
+  for (uint64_t i = 0; i < count; ++i) seen[tokens[i] / 8] &= (uint8_t)~(1u << (tokens[i] & 7));
+  if (out) *out = row.selected;
+  return PB_OK;
+}
+
+uint32_t pb_greedy_token(const uint32_t* logits, uint64_t len, uint32_t* out, pb_error* err) {
+  uint32_t st = validate_logits(logits, len, err);
+  if (st) return st;
+  RowScratch s;
+  PB_CUDA(cudaMalloc(&s.logits, kV * 4));
+  PB_CUDA(cudaMalloc(&s.ids, 8));
+  PB_CUDA(cudaMemcpy(s.logits, logits, kV * 4, cudaMemcpyHostToDevice));
+  pb::launch_argmax(s.logits, kV, 1, (int)kV, s.ids, s.ids + 1, nullptr, nullptr);
+  PB_CUDA(cudaGetLastError());
+  uint32_t host[2];
+  PB_CUDA(cudaMemcpy(host, s.ids, 8, cudaMemcpyDeviceToHost));
+  if (out) *out = host[0];
+  return PB_OK;
+}
+
+uint32_t pb_top_logits_8(const uint32_t* logits, uint64_t len, pb_top_logit* out8, pb_error* err) {
+  uint32_t st = validate_logits(logits, len, err);
+  if (st) return st;
+  RowScratch s;
+  PB_CUDA(cudaMalloc(&s.logits, kV * 4));
+  PB_CUDA(cudaMalloc(&s.pairs, 16 * 4));
+  PB_CUDA(cudaMemcpy(s.logits, logits, kV * 4, cudaMemcpyHostToDevice));
+  pb::launch_topk8(s.logits, kV, 1, (int)kV, s.pairs, nullptr, nullptr);
+  PB_CUDA(cudaGetLastError());
+  uint32_t host[16];
+  PB_CUDA(cudaMemcpy(host, s.pairs, sizeof host, cudaMemcpyDeviceToHost));
+  for (int i = 0; i < 8; ++i) out8[i] = pb_top_logit{host[2 * i], host[2 * i + 1]};
+  return PB_OK;
+}
+
+uint32_t pb_sample_batch_device(uint32_t* logits_device, uint64_t ld, uint32_t rows,
+                                const uint32_t* history_device, const uint64_t* offsets_device,
+                                const uint32_t* lengths_device, pb_sampling_state* states_device,
+                                uint32_t* out_device, void* stream) {
+  if (!logits_device || rows == 0 || ld < kV || (ld & 3)) return PB_CAPACITY;
+  pb::launch_sampler(reinterpret_cast<float*>(logits_device), ld, (int)rows, (int)kV,
+                     history_device, offsets_device, lengths_device, nullptr,
+                     reinterpret_cast<unsigned long long*>(states_device),
+                     reinterpret_cast<pb::SamplerRow*>(out_device), (cudaStream_t)stream);
+  PB_CUDA(cudaGetLastError());
+  return PB_OK;
+}
+
+uint32_t pb_qmatvec_device(uint32_t wtype, const uint8_t* w, uint32_t rows, uint32_t cols,
+                           const float* x, uint32_t batch, float* y, void* stream) {
+  const uint32_t nb = cols / 32;
+  const uint32_t rt = nb > 64 ? 8 : 32;
+  if ((wtype != pb::W_Q4_0 && wtype != pb::W_Q8_0) || cols % 32 || cols > (uint32_t)pb::kFfn ||
+      rows == 0 || rows % rt || batch == 0)
+    return PB_CAPACITY;
+  cudaStream_t s = (cudaStream_t)stream;
+  pb::init_kernel_attributes();
+  OpScratch scr(s);
+  PB_CUDA(scr.alloc(batch));
+  pb::Batch b = scr.batch(batch);
+  pb::launch_quant(b, x, cols, (int)cols, s);
+  pb::Epilogue ep{pb::EPI_STORE, y, rows, nullptr, scr.err, 0, 0};
+  pb::launch_qgemv((int)wtype, w, (int)rows, (int)cols, b, ep, s);
+  PB_CUDA(cudaGetLastError());
+  return PB_OK;
+}
+
+uint32_t pb_quantize_q8_device(const float* x, uint32_t rows, uint32_t cols, uint8_t* staging,
+                               void* stream) {
+  if (cols % 32 || cols > (uint32_t)pb::kFfn || rows == 0) return PB_CAPACITY;
+  cudaStream_t s = (cudaStream_t)stream;
+  OpScratch scr(s);
+  PB_CUDA(scr.alloc(rows));
+  pb::Batch b = scr.batch(rows);
+  pb::launch_quant(b, x, cols, (int)cols, s);
+  const int total = (int)(rows * (cols / 32));
+  staging_kernel<<<(total + 127) / 128, 128, 0, s>>>(scr.aq, scr.ad, (int)rows, (int)(cols / 32), staging);
+  PB_CUDA(cudaGetLastError());
+  return PB_OK;
+}
+
+uint32_t pb_rmsnorm_device(const float* x, const float* w, uint32_t rows, float* y, void* stream) {
+  if (rows == 0) return PB_CAPACITY;
+  cudaStream_t s = (cudaStream_t)stream;
+  OpScratch scr(s);
+  PB_CUDA(scr.alloc(rows));
+  pb::Batch b = scr.batch(rows);
+  b.hidden = const_cast<float*>(x);
+  b.norm_out = y;
+  pb::launch_rmsnorm_quant(b, w, 1, pb::D_ATTN_NORM, s);
+  PB_CUDA(cudaGetLastError());
+  return PB_OK;
+}
+
+uint32_t pb_swiglu_device(const float* gate, const float* up, uint32_t rows, float* out,
+                          void* stream) {
+  if (rows == 0) return PB_CAPACITY;
+  cudaStream_t s = (cudaStream_t)stream;
+  OpScratch scr(s);
+  PB_CUDA(scr.alloc(rows));
+  pb::Batch b = scr.batch(rows);
+  b.gate = const_cast<float*>(gate);
+  b.up = const_cast<float*>(up);
+  b.product_out = out;
+  pb::launch_swiglu_quant(b, 1, s);
+  PB_CUDA(cudaGetLastError());
+  return PB_OK;
+}
+
+uint32_t pb_rope_kv_device(float* q, float* k, const float* v, const uint32_t* positions_host,
+                           uint32_t rows, float* kv, uint32_t capacity, uint32_t layer,
+                           void* stream) {
+  if (rows == 0 || capacity == 0 || (capacity & 3) || layer >= 24) return PB_CAPACITY;
+  for (uint32_t r = 0; r < rows; ++r) if (positions_host[r] >= capacity) return PB_CAPACITY;
+  cudaStream_t s = (cudaStream_t)stream;
+  std::vector<float> table;
+  pb::build_rope_table(table);
+  float* rope = nullptr;
+  PB_CUDA(cudaMallocAsync(&rope, table.size() * 4, s));
+  PB_CUDA(cudaMemcpyAsync(rope, table.data(), table.size() * 4, cudaMemcpyHostToDevice, s));
+  OpScratch scr(s);
+  PB_CUDA(scr.alloc(rows));
+  PB_CUDA(cudaMemcpyAsync(scr.positions, positions_host, rows * 4, cudaMemcpyHostToDevice, s));
+  pb::Batch b = scr.batch(rows);
+  b.q = q; b.k = k; b.v = const_cast<float*>(v); b.kv = kv; b.capacity = capacity;
+  pb::launch_rope_kv(b, (int)layer, rope, s);
+  PB_CUDA(cudaGetLastError());
+  PB_CUDA(cudaStreamSynchronize(s));
+  PB_CUDA(cudaFree(rope));
+  return PB_OK;
+}
+
+uint32_t pb_attention_device(const float* q, const float* kv, uint32_t capacity, uint32_t layer,
+                             const uint32_t* positions_host, uint32_t rows, uint32_t span,
+                             float* out, float* scores, void* stream) {
+  if (rows == 0 || capacity == 0 || (capacity & 3) || layer >= 24 || (span & 3)) return PB_CAPACITY;
+  uint32_t span_max = span;
+  for (uint32_t r = 0; r < rows; ++r) {
+    if (positions_host[r] >= capacity) return PB_CAPACITY;
+    span_max = std::max<uint32_t>(span_max, (positions_host[r] + 4) & ~3u);
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  OpScratch scr(s);
+  PB_CUDA(scr.alloc(rows));
+  PB_CUDA(cudaMemcpyAsync(scr.positions, positions_host, rows * 4, cudaMemcpyHostToDevice, s));
+  float* sc = scores;
+  if (!sc) PB_CUDA(cudaMallocAsync(&sc, (size_t)rows * 14 * span_max * 4, s));
+  pb::Batch b = scr.batch(rows);
+  b.q = const_cast<float*>(q); b.kv = const_cast<float*>(kv); b.capacity = capacity;
+  b.attn = out; b.scores = sc; b.score_stride = span_max; b.span_min = (int)span;
+  pb::launch_attention(b, (int)layer, s);
+  PB_CUDA(cudaGetLastError());
+  if (!scores) PB_CUDA(cudaFreeAsync(sc, s));
+  return PB_OK;
+}
+
+}  // extern "C"

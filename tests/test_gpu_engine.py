@@ -1,0 +1,204 @@
+"""End-to-end engine parity on the GPU against the CPU oracle's restatement of
+inference.rs:1454-1765, plus the state machine and error semantics of
+inference.rs:967-1371 and host-side fault injection (a NaN planted in a weight
+of the model image, never a device fault)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from promptboot_b200 import api, pbtqw25
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+NO = 0xFFFFFFFF
+CAP = 256
+
+
+def prompt(n, seed=0x5EED0000):
+    return np.random.default_rng(seed).integers(0, 151643, size=n, dtype=np.uint32)
+
+
+@pytest.fixture(scope="module")
+def engine(model_view):
+    e = api.InferenceEngine(model_view, max_seqs=4, max_context=CAP)
+    yield e
+    e.close()
+
+
+def oracle_prefill_logits(model_image, tokens):
+    kv = np.zeros(24 * 2 * 2 * CAP * 64, dtype=np.float32)
+    logits = None
+    for i, t in enumerate(tokens):
+        st, logits, err = oracle.forward(model_image, kv, CAP, int(t), i, i + 1 == len(tokens))
+        assert st == 0
+    return logits, kv
+
+
+def test_prefill_and_decode_logits_bit_exact(engine, model_image):
+    toks = prompt(6)
+    engine.reset(0)
+    logits = np.zeros(api.VOCAB, dtype=np.uint32)
+    step = engine.prefill(toks, 8, logits)
+    ref, kv = oracle_prefill_logits(model_image, toks)
+    assert np.array_equal(logits, ref.view(np.uint32))
+    assert step.position == 6 and step.selected_token == oracle.argmax(ref)
+    assert step.selected_logit_bits == int(ref.view(np.uint32)[step.selected_token])
+    # decode_selected of an arbitrary token, then decode of the greedy one
+    for i, token in enumerate([12345, None, None]):
+        token = step.selected_token if token is None else token
+        fn = engine.decode if i else engine.decode_selected
+        step = fn(token, logits)
+        st, ref, _ = oracle.forward(model_image, kv, CAP, token, 6 + i, True)
+        assert st == 0
+        assert np.array_equal(logits, ref.view(np.uint32)), i
+        assert step.selected_token == oracle.argmax(ref) and step.position == 7 + i
+
+
+def test_repl_generation_matches_oracle(engine, model_image):
+    """src/model_repl.rs:927-1000 semantics: sample with the full history after
+    every step, then decode_selected(sampled)."""
+    toks = prompt(5, seed=3)
+    engine.reset(1)
+    logits = np.zeros(api.VOCAB, dtype=np.uint32)
+    engine.prefill(toks, 16, logits, seq=1)
+    seen = np.zeros(api.SEEN_BYTES, dtype=np.uint8)
+    state = api.SamplingState(1)
+    history = list(toks)
+    got = []
+    for i in range(6):
+        sel = api.sample_token_with_repetition(logits, history, seen, state)
+        got.append(sel)
+        history.append(sel)
+        if i < 5:
+            engine.decode_selected(sel, logits, seq=1)
+    st, ref_tokens, _, _ = oracle.generate(model_image, toks, 6, 1, CAP)
+    assert st == 0
+    assert got == list(ref_tokens)
+    assert state.draws() == 6
+
+
+def test_batched_device_generation_matches_oracle(model_view, model_image):
+    e = api.InferenceEngine(model_view, max_seqs=3, max_context=64)
+    prompts = np.stack([prompt(7, seed=s) for s in (10, 11, 12)])
+    status, steps, errs = e.prefill_batch([0, 1, 2], prompts, 32)
+    assert status == 0
+    states = [api.SamplingState(s) for s in (0, 5, 9)]
+    status, out, errs = e.generate([0, 1, 2], states, 5)
+    assert status == 0
+    for i, seed in enumerate((0, 5, 9)):
+        st, ref, _, _ = oracle.generate(model_image, prompts[i], 5, seed, 64)
+        assert st == 0 and list(out[:, i]) == list(ref), i
+        assert states[i].draws() == 5
+        assert e.position(i) == 7 + 5
+    e.close()
+
+
+def test_engine_sample_matches_host_sampler(model_view):
+    e = api.InferenceEngine(model_view, max_seqs=2, max_context=64)
+    prompts = np.stack([prompt(4, seed=20), prompt(4, seed=21)])
+    assert e.prefill_batch([0, 1], prompts, 8)[0] == 0
+    rows = [e.logits(0), e.logits(1)]
+    states = [api.SamplingState(7), api.SamplingState(8)]
+    st, ids, errs = e.sample([0, 1], states)
+    assert st == 0
+    for i in range(2):
+        ref_state = api.SamplingState(7 + i)
+        seen = np.zeros(api.SEEN_BYTES, dtype=np.uint8)
+        ref = api.sample_token_with_repetition(rows[i].copy(), prompts[i], seen, ref_state)
+        assert ids[i] == ref and states[i] == ref_state
+    e.close()
+
+
+def test_state_machine_errors_match_reference(model_view):
+    """inference.rs:1026-1371 prechecks (tests.rs:883-1768 shapes, synthetic model)."""
+    e = api.InferenceEngine(model_view, max_seqs=1, max_context=64)
+    logits = np.zeros(api.VOCAB, dtype=np.uint32)
+    with pytest.raises(api.InferenceError) as x:
+        e.decode_selected(1, logits)
+    assert x.value.tuple() == [1, 2, NO, 0, NO, 1, 0, (1 << 32) | 0]
+    with pytest.raises(api.InferenceError) as x:
+        e.append_prefill([1], 4, logits)
+    assert x.value.tuple() == [1, 2, NO, 0, NO, 1, 0, (1 << 32) | 0]
+    with pytest.raises(api.InferenceError) as x:
+        e.prefill([1, 2], 0, logits)
+    assert x.value.tuple() == [2, 2, NO, 0, NO, 1, 0, (11 << 32) | 0]
+    with pytest.raises(api.InferenceError) as x:
+        e.prefill([], 4, logits)
+    assert x.value.tuple() == [2, 2, NO, 0, NO, 1, 0, (3 << 32) | 0]
+    with pytest.raises(api.InferenceError) as x:
+        e.prefill([1, 2, 3], 62, logits)
+    assert x.value.tuple() == [2, 2, NO, 0, NO, 64, 65, (3 << 32) | 1]
+    with pytest.raises(api.InferenceError) as x:
+        e.prefill([1, 151936], 4, logits)
+    assert x.value.tuple() == [3, 2, NO, 1, NO, 151936, 151936, (2 << 32) | 0]
+    assert e.usage().state == 0 and e.position() == 0
+    step = e.prefill([5, 6, 7], 2, logits)
+    assert e.usage().state in (1, 2) and e.position() == 3
+    with pytest.raises(api.InferenceError) as x:
+        e.prefill([1], 4, logits)
+    assert x.value.tuple()[:2] == [1, 2] and x.value.detail == (1 << 32) | 1
+    wrong = (step.selected_token + 1) % api.VOCAB
+    with pytest.raises(api.InferenceError) as x:
+        e.decode(wrong, logits)
+    assert x.value.tuple() == [1, 19, NO, 3, NO, step.selected_token, wrong, (14 << 32) | 0]
+    with pytest.raises(api.InferenceError) as x:
+        e.decode_selected(151936, logits)
+    assert x.value.tuple() == [3, 2, NO, 3, NO, 151936, 151936, (2 << 32) | 1]
+    e.decode_selected(9, logits)  # second prediction of reserve 2
+    with pytest.raises(api.InferenceError) as x:
+        e.decode_selected(9, logits)
+    assert x.value.tuple() == [2, 2, NO, 4, NO, 2, 2, (11 << 32) | 1]
+    u = e.usage()
+    assert (u.position, u.context_limit, u.generation_reserve) == (4, 64, 2)
+    assert u.kv.current == 4 * 24576 and u.kv.high_water == 4 * 24576
+    e.reset()
+    assert e.usage().state == 0 and e.position() == 0
+    e.close()
+
+
+def test_retained_prefix_reuse_is_exact(model_view, model_image):
+    """prefill_with_prefix / reset_to_prefix (inference.rs:1044-1093, 1315-1335)."""
+    e = api.InferenceEngine(model_view, max_seqs=1, max_context=64)
+    a = np.concatenate([prompt(4, seed=30), prompt(3, seed=31)])
+    b = np.concatenate([a[:4], prompt(2, seed=32)])
+    logits = np.zeros(api.VOCAB, dtype=np.uint32)
+    e.prefill_with_prefix(a, 4, 8, logits)
+    e.decode_selected(17, logits)
+    assert e.reset_to_prefix() == 4 and e.position() == 4
+    e.prefill_with_prefix(b, 4, 8, logits)
+    ref, _ = oracle_prefill_logits(model_image, b)
+    assert np.array_equal(logits, ref.view(np.uint32))
+    with pytest.raises(api.InferenceError) as x:
+        e.prefill_with_prefix(b, 0, 8, logits)
+    assert x.value.tuple() == [2, 2, NO, 0, NO, 1, 0, (3 << 32) | 3]
+    assert e.position() == 0 and e.reset_to_prefix() == 0
+    e.close()
+
+
+def test_nonfinite_weight_faults_with_reference_error(model_image):
+    """inference.rs:1889-1944: a NaN in layer 2's FFN norm weight faults the FFN_NORM
+    stage of layer 2 at element 5; logits are zeroed and only reset recovers."""
+    img = model_image.copy()
+    tid = pbtqw25.layer_tensor(2, 14)
+    off = int(np.frombuffer(img[pbtqw25.TENSOR_DIR + tid * 96 + 32:][:8].tobytes(), np.uint64)[0])
+    img[off + 5 * 4:off + 6 * 4] = np.frombuffer(np.uint32(0x7FC00000).tobytes(), np.uint8)
+    view = api.ModelView(img)
+    e = api.InferenceEngine(view, max_seqs=1, max_context=64)
+    logits = np.ones(api.VOCAB, dtype=np.uint32)
+    with pytest.raises(api.InferenceError) as x:
+        e.prefill([1, 2, 3], 4, logits)
+    # status, domain, layer, position, tensor and index are the reference's; the
+    # NaN's payload is the GPU's canonical NaN rather than x86's propagated one.
+    t = x.value.tuple()
+    assert t[:6] == [6, 12, 2, 0, tid, 0] and t[7] == (7 << 32) | 5
+    assert t[6] & 0x7F800000 == 0x7F800000 and t[6] & 0x7FFFFF
+    assert not logits.any()
+    assert e.usage().state == 3
+    with pytest.raises(api.InferenceError) as x:
+        e.decode_selected(1, logits)
+    assert x.value.tuple()[:2] == [1, 2] and x.value.detail == (1 << 32) | 3
+    e.close()
+    view.close()

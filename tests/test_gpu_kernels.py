@@ -1,0 +1,216 @@
+"""Kernel parity on the GPU: each sm_100a kernel against the reference's golden
+vectors (tests/golden) and against the CPU oracle on seeded random inputs.
+The bar is bit-exact binary32 output."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import dev, ptr
+from promptboot_b200 import _lib
+from test_oracle_golden import (GOLDEN, attention_fixture_kv, attention_query, dot_inputs,
+                                quant_input)
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def sync():
+    torch.cuda.synchronize()
+
+
+def host(t) -> np.ndarray:
+    return t.cpu().numpy()
+
+
+def u32(a) -> np.ndarray:
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+def test_quantizer_matches_fixture_and_oracle():
+    lib = _lib.load()
+    x = quant_input()[None, :]
+    out = torch.zeros(6 * 34, dtype=torch.uint8, device="cuda")
+    assert lib.pb_quantize_q8_device(ptr(dev(x)), 1, 192, ptr(out), None) == 0
+    sync()
+    assert host(out).tobytes() == (GOLDEN / "q8.bin").read_bytes()
+    rng = np.random.default_rng(11)
+    for cols in (896, 4864):
+        x = (rng.standard_normal((5, cols)) * rng.choice([1e-3, 1.0, 40.0], size=(5, 1))).astype(np.float32)
+        x[0, :32] = 0.0
+        out = torch.zeros(5 * cols // 32 * 34, dtype=torch.uint8, device="cuda")
+        assert lib.pb_quantize_q8_device(ptr(dev(x)), 5, cols, ptr(out), None) == 0
+        sync()
+        got = host(out).reshape(5, -1)
+        for r in range(5):
+            assert np.array_equal(got[r], oracle.prepare_q8(x[r])), (cols, r)
+
+
+def test_rmsnorm_matches_fixture_and_oracle():
+    lib = _lib.load()
+    x = np.array([((i % 17) - 8) / 8.0 for i in range(896)], dtype=np.float32)
+    w = np.array([((i % 7) + 1) / 4.0 for i in range(896)], dtype=np.float32)
+    rng = np.random.default_rng(5)
+    xs = np.stack([x] + [rng.standard_normal(896).astype(np.float32) * s for s in (1e-3, 1.0, 30.0)])
+    y = torch.zeros((4, 896), dtype=torch.float32, device="cuda")
+    assert lib.pb_rmsnorm_device(ptr(dev(xs)), ptr(dev(w)), 4, ptr(y), None) == 0
+    sync()
+    got = host(y)
+    assert got[0].tobytes() == (GOLDEN / "rms.bin").read_bytes()
+    for r in range(4):
+        assert np.array_equal(u32(got[r]), u32(oracle.rmsnorm(xs[r], w)))
+
+
+def test_swiglu_matches_fixture_and_oracle():
+    lib = _lib.load()
+    g = np.array([((i % 33) - 16) / 16.0 for i in range(4864)], dtype=np.float32)
+    u = np.array([((i % 19) - 9) / 8.0 for i in range(4864)], dtype=np.float32)
+    rng = np.random.default_rng(9)
+    g2 = (rng.standard_normal(4864) * 30).astype(np.float32)
+    g2[:4] = [-200.0, 200.0, 0.0, -0.0]
+    u2 = rng.standard_normal(4864).astype(np.float32)
+    out = torch.zeros((2, 4864), dtype=torch.float32, device="cuda")
+    assert lib.pb_swiglu_device(ptr(dev(np.stack([g, g2]))), ptr(dev(np.stack([u, u2]))), 2,
+                                ptr(out), None) == 0
+    sync()
+    got = host(out)
+    assert got[0].tobytes() == (GOLDEN / "swiglu.bin").read_bytes()
+    assert np.array_equal(u32(got[1]), u32(oracle.swiglu(g2, u2)))
+
+
+def test_rope_and_kv_write_match_fixture_and_oracle():
+    lib = _lib.load()
+    cap = 1024
+    rng = np.random.default_rng(2)
+    q = rng.standard_normal((2, 896)).astype(np.float32)
+    q[0, :64] = [(i - 32) / 16.0 for i in range(64)]
+    k = rng.standard_normal((2, 128)).astype(np.float32)
+    v = rng.standard_normal((2, 128)).astype(np.float32)
+    positions = np.array([511, 1023], dtype=np.uint32)
+    kv = torch.zeros(2 * 24 * 4 * cap * 64, dtype=torch.float32, device="cuda")
+    qd, kd = dev(q), dev(k)
+    assert lib.pb_rope_kv_device(ptr(qd), ptr(kd), ptr(dev(v)), positions.ctypes.data_as(ctypes.c_void_p),
+                                 2, ptr(kv), cap, 5, None) == 0
+    sync()
+    gq, gk, gkv = host(qd), host(kd), host(kv)
+    assert gq[0, :64].tobytes() == (GOLDEN / "rope.bin").read_bytes()
+    for r in range(2):
+        assert np.array_equal(u32(gq[r]), u32(oracle.rope_in_place(q[r], 14, int(positions[r]))))
+        kr = oracle.rope_in_place(k[r], 2, int(positions[r]))
+        assert np.array_equal(u32(gk[r]), u32(kr))
+        base = r * 24 * 4 * cap * 64
+        for h in range(2):
+            for c in range(64):
+                kw = oracle.kv_word(cap, 5, 0, int(positions[r]), h, c)
+                vw = oracle.kv_word(cap, 5, 1, int(positions[r]), h, c)
+                assert u32(gkv[base + kw:base + kw + 1])[0] == u32(kr[h * 64 + c:h * 64 + c + 1])[0]
+                assert gkv[base + vw] == v[r, h * 64 + c]
+
+
+@pytest.mark.parametrize("current,span,fixture,rot", [(2, 256, "256", 0), (256, 512, "512", 7)])
+def test_attention_matches_fixtures(current, span, fixture, rot):
+    lib = _lib.load()
+    cap = 32768
+    kv = attention_fixture_kv(cap)
+    q = np.roll(attention_query(), -rot)
+    out = torch.zeros(896, dtype=torch.float32, device="cuda")
+    scores = torch.zeros(14 * span, dtype=torch.float32, device="cuda")
+    pos = np.array([current], dtype=np.uint32)
+    assert lib.pb_attention_device(ptr(dev(q)), ptr(dev(kv)), cap, 0,
+                                   pos.ctypes.data_as(ctypes.c_void_p), 1, span, ptr(out),
+                                   ptr(scores), None) == 0
+    sync()
+    assert host(out).tobytes() == (GOLDEN / f"attention-{fixture}.bin").read_bytes()
+    last_head = host(scores)[13 * span:14 * span]
+    assert last_head.tobytes() == (GOLDEN / f"scores-{fixture}.bin").read_bytes()
+
+
+@pytest.mark.parametrize("positions", [[0, 1, 2], [3, 4, 5], [29, 255, 256], [511, 512, 600]])
+def test_attention_random_kv_matches_oracle(positions):
+    """Edge spans (1..N positions, masked tails) and the reference's denormal /
+    signed-zero query words (tests.rs:699-706)."""
+    lib = _lib.load()
+    cap = 1024
+    rows = len(positions)
+    rng = np.random.default_rng(sum(positions))
+    kv = np.zeros(rows * 24 * 4 * cap * 64, dtype=np.float32)
+    layer = 3
+    for r in range(rows):
+        base = r * 24 * 4 * cap * 64 + layer * 4 * cap * 64
+        kv[base:base + 4 * cap * 64] = rng.standard_normal(4 * cap * 64).astype(np.float32)
+    q = rng.standard_normal((rows, 896)).astype(np.float32)
+    q[0, :6] = oracle.f32([0x00000000, 0x80000000, 0x00000001, 0x007FFFFF, 0x00800000, 0x80000001])
+    out = torch.zeros((rows, 896), dtype=torch.float32, device="cuda")
+    pos = np.array(positions, dtype=np.uint32)
+    assert lib.pb_attention_device(ptr(dev(q)), ptr(dev(kv)), cap, layer,
+                                   pos.ctypes.data_as(ctypes.c_void_p), rows, 0, ptr(out), None,
+                                   None) == 0
+    sync()
+    got = host(out)
+    for r in range(rows):
+        kvr = kv[r * 24 * 4 * cap * 64:(r + 1) * 24 * 4 * cap * 64]
+        span = (positions[r] + 4) & ~3
+        ref, _ = oracle.attention(q[r], kvr, cap, layer, positions[r], span)
+        assert np.array_equal(u32(got[r]), u32(ref)), (r, positions[r])
+
+
+def _q4_weights(rng, rows, cols):
+    nb = rows * cols // 32
+    scales = (np.abs(rng.standard_normal(nb) * 0.02) / 8).astype(np.float16)
+    nib = rng.integers(0, 16, size=(nb, 32), dtype=np.uint8)
+    w = np.empty((nb, 18), dtype=np.uint8)
+    w[:, :2] = scales.view(np.uint8).reshape(nb, 2)
+    w[:, 2:] = nib[:, :16] | (nib[:, 16:] << 4)
+    return w.reshape(-1)
+
+
+def _q8_weights(rng, rows, cols):
+    nb = rows * cols // 32
+    scales = (np.abs(rng.standard_normal(nb) * 0.02) / 8).astype(np.float16)
+    w = np.empty((nb, 34), dtype=np.uint8)
+    w[:, :2] = scales.view(np.uint8).reshape(nb, 2)
+    w[:, 2:] = rng.integers(-128, 128, size=(nb, 32), dtype=np.int8).view(np.uint8)
+    return w.reshape(-1)
+
+
+def test_matvec_dot_fixture():
+    lib = _lib.load()
+    mat, q4, q8 = dot_inputs()
+    rng = np.random.default_rng(1)
+    w4 = np.concatenate([q4, _q4_weights(rng, 31, 64)])
+    w8 = np.concatenate([q8, _q8_weights(rng, 31, 64)])
+    y = torch.zeros(32, dtype=torch.float32, device="cuda")
+    x = dev(mat[None, :])
+    assert lib.pb_qmatvec_device(2, ptr(dev(w4)), 32, 64, ptr(x), 1, ptr(y), None) == 0
+    sync()
+    y4 = host(y).copy()
+    assert lib.pb_qmatvec_device(3, ptr(dev(w8)), 32, 64, ptr(x), 1, ptr(y), None) == 0
+    sync()
+    y8 = host(y).copy()
+    assert u32(y4[:1])[0] == 0x43E08000 and u32(y8[:1])[0] == 0x44388000
+    st = oracle.prepare_q8(mat)
+    assert np.array_equal(u32(y4), u32(oracle.q4_matvec(w4, st, 32, 64)))
+    assert np.array_equal(u32(y8), u32(oracle.q8_matvec(w8, st, 32, 64)))
+
+
+@pytest.mark.parametrize("wtype,rows,cols", [(2, 896, 896), (2, 128, 896), (2, 4864, 896),
+                                             (2, 896, 4864), (3, 151936, 896)])
+@pytest.mark.parametrize("batch", [1, 8, 9])
+def test_matvec_shapes_match_oracle(wtype, rows, cols, batch):
+    lib = _lib.load()
+    rng = np.random.default_rng(rows * 7 + cols + batch)
+    w = _q4_weights(rng, rows, cols) if wtype == 2 else _q8_weights(rng, rows, cols)
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    y = torch.zeros((batch, rows), dtype=torch.float32, device="cuda")
+    assert lib.pb_qmatvec_device(wtype, ptr(dev(w)), rows, cols, ptr(dev(x)), batch, ptr(y), None) == 0
+    sync()
+    got = host(y)
+    check_rows = range(batch) if rows * batch <= 8 * 151936 else [0, batch - 1]
+    for b in check_rows:
+        st = oracle.prepare_q8(x[b])
+        ref = oracle.q4_matvec(w, st, rows, cols) if wtype == 2 else oracle.q8_matvec(w, st, rows, cols)
+        assert np.array_equal(u32(got[b]), u32(ref)), b

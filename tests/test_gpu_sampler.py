@@ -1,0 +1,168 @@
+"""Sampler parity on the GPU: the reference's known-answer tests
+(tests.rs:368-599) through the host-buffer API, and a config-1-style batch
+(N(0, 3^2) rows, five raised positions, 512-token histories, seed 7) through
+the device batch API, every sampled id bit-exact to the CPU oracle."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import dev, ptr
+from promptboot_b200 import _lib, api
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+V = api.VOCAB
+
+
+def f32bits(x) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(x, dtype=np.float32)).view(np.uint32)
+
+
+def kat_logits():
+    logits = np.full(V, -100.0, dtype=np.float32)
+    for t in range(41):
+        logits[t] = np.float32(4.0) - np.float32(t) * np.float32(0.05)
+    return logits
+
+
+def test_greedy_lowest_id_on_ties():
+    logits = np.full(V, -100.0, dtype=np.float32)
+    logits[7] = logits[3] = 1.5
+    assert api.greedy_token(f32bits(logits)) == 3
+
+
+def test_sampling_known_answer_state():
+    logits = f32bits(kat_logits())
+    first = api.SamplingState(0x0123456789ABCDEF)
+    second = first.copy()
+    ref = oracle.SamplingState(0x0123456789ABCDEF)
+    for _ in range(8):
+        a = api.sample_token(logits, first)
+        assert a == api.sample_token(logits, second)
+        assert a == oracle.sample_top_k_top_p(kat_logits(), ref.next_24())
+        assert a < 20
+    assert first == second and first.draws() == 8
+    assert first.state() == 0x37FE8664CE109D2F
+
+
+def test_repetition_penalty_known_answer():
+    logits = np.zeros(V, dtype=np.float32)
+    logits[7], logits[9], logits[12] = 11.0, -2.0, np.float32(-0.0)
+    bits = f32bits(logits).copy()
+    seen = np.zeros(api.SEEN_BYTES, dtype=np.uint8)
+    st = api.SamplingState(1)
+    api.sample_token_with_repetition(bits, [7, 9, 7, 12, 9], seen, st)
+    assert bits[7] == f32bits(np.float32(11.0) / np.float32(1.1))
+    assert bits[9] == f32bits(np.float32(-2.0) * np.float32(1.1))
+    assert bits[12] == 0x80000000
+    assert not seen.any() and st.draws() == 1
+
+
+def test_dirty_seen_bitmap_follows_reference():
+    """A token already marked in `seen` is not penalised, and is cleared after."""
+    logits = np.linspace(-3, 3, V).astype(np.float32)
+    a, b = f32bits(logits).copy(), logits.copy()
+    seen_a = np.zeros(api.SEEN_BYTES, dtype=np.uint8)
+    seen_a[5 // 8] |= 1 << (5 % 8)
+    seen_b = seen_a.copy()
+    s1, s2 = api.SamplingState(3), oracle.SamplingState(3)
+    got = api.sample_token_with_repetition(a, [5, 6, 151935], seen_a, s1)
+    status, ref, _ = oracle.sample_with_repetition(b, [5, 6, 151935], s2, seen_b)
+    assert status == 0 and got == ref
+    assert np.array_equal(a, f32bits(b)) and np.array_equal(seen_a, seen_b)
+
+
+def test_dominant_eos_collapses_top_p():
+    logits = np.full(V, -100.0, dtype=np.float32)
+    logits[151645] = 10.0
+    logits[9] = 0.0
+    for seed in (0, 1, 2**64 - 1, 0xFEEDFACEDEADBEEF):
+        st = api.SamplingState(seed)
+        assert api.sample_token(f32bits(logits), st) == 151645 and st.draws() == 1
+
+
+def test_top_logits_8_order_and_signed_zero():
+    logits = np.full(V, -100.0, dtype=np.float32)
+    for t, v in [(7, 9.0), (2, 9.0), (11, 8.0), (4, 7.0), (15, 6.0), (5, 5.0), (20, 4.0),
+                 (6, 3.0), (30, 2.0)]:
+        logits[t] = v
+    got = api.top_logits_8(f32bits(logits))
+    assert got == [(t, int(f32bits(np.float32(v)))) for t, v in
+                   [(2, 9.0), (7, 9.0), (11, 8.0), (4, 7.0), (15, 6.0), (5, 5.0), (20, 4.0), (6, 3.0)]]
+    logits = np.full(V, -100.0, dtype=np.float32)
+    logits[1:9] = [-0.0, 0.0, -1, -2, -3, -4, -5, -6]
+    got = api.top_logits_8(f32bits(logits))
+    assert [t for t, _ in got] == [1, 2, 3, 4, 5, 6, 7, 8]
+    assert got[0][1] == 0x80000000 and got[1][1] == 0
+
+
+def config1_batch(rows: int, seed: int = 7):
+    rng = np.random.default_rng(seed)
+    logits = (rng.standard_normal((rows, V)) * 3.0).astype(np.float32)
+    for r in range(rows):
+        logits[r, rng.choice(V, size=5, replace=False)] += np.float32(12.0)
+    history = rng.integers(0, V, size=(rows, 512), dtype=np.uint32)
+    return logits, history
+
+
+@pytest.mark.parametrize("rows", [1, 256])
+def test_device_batch_sampler_matches_oracle(rows):
+    logits, history = config1_batch(rows)
+    lib = _lib.load()
+    d_logits = dev(logits)
+    d_hist = dev(history.reshape(-1))
+    offsets = np.arange(rows, dtype=np.uint64) * 512
+    lengths = np.full(rows, 512, dtype=np.uint32)
+    # one SamplingState(7) drawn once per row in row order (row r uses draw r+1)
+    master = oracle.SamplingState(7)
+    states = np.zeros((rows, 2), dtype=np.uint64)
+    draws = []
+    for r in range(rows):
+        st_before = int(master.state[0])
+        draws.append(master.next_24())
+        states[r] = [st_before, r]
+    d_states = dev(states)
+    out = torch.zeros((rows, 4), dtype=torch.int32, device="cuda")
+    assert lib.pb_sample_batch_device(ptr(d_logits), V, rows, ptr(d_hist), ptr(dev(offsets)),
+                                      ptr(dev(lengths)), ptr(d_states), ptr(out), None) == 0
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint32)
+    mutated = d_logits.cpu().numpy()
+    for r in range(rows):
+        ref_logits = logits[r].copy()
+        seen = np.zeros(api.SEEN_BYTES, dtype=np.uint8)
+        oracle.lib().orc_apply_repetition_penalty(oracle._p(ref_logits), oracle._p(history[r]),
+                                                  512, oracle._p(seen))
+        ref = oracle.sample_top_k_top_p(ref_logits, draws[r])
+        assert got[r, 0] == 0 and got[r, 3] == ref, r
+        assert got[r, 2] == draws[r]
+        assert np.array_equal(f32bits(mutated[r]), f32bits(ref_logits)), r
+
+
+def test_device_batch_sampler_rejects_rows_transactionally():
+    logits, history = config1_batch(3, seed=8)
+    logits[1, 1234] = np.inf
+    history[2, 17] = V + 5
+    lib = _lib.load()
+    d_logits = dev(logits)
+    states = np.array([[11, 0], [12, 0], [13, 0]], dtype=np.uint64)
+    d_states = dev(states)
+    out = torch.zeros((3, 4), dtype=torch.int32, device="cuda")
+    assert lib.pb_sample_batch_device(ptr(d_logits), V, 3, ptr(dev(history.reshape(-1))),
+                                      ptr(dev(np.arange(3, dtype=np.uint64) * 512)),
+                                      ptr(dev(np.full(3, 512, dtype=np.uint32))), ptr(d_states),
+                                      ptr(out), None) == 0
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint32)
+    st = d_states.cpu().numpy().view(np.uint64)
+    assert got[0, 0] == 0 and st[0, 1] == 1
+    assert list(got[1, :3]) == [7, 1234, 0x7F800000] and list(st[1]) == [12, 0]
+    assert list(got[2, :3]) == [3, 17, V + 5] and list(st[2]) == [13, 0]
+    after = d_logits.cpu().numpy()
+    assert np.array_equal(f32bits(after[1]), f32bits(logits[1]))
+    assert np.array_equal(f32bits(after[2]), f32bits(logits[2]))
