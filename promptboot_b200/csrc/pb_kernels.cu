@@ -76,9 +76,10 @@ __device__ __forceinline__ void quantize_block_warp(float x, int8_t* aq, float* 
 
 // fp32_sse2.rs:1310-1334 then the quantizer.  The f64 sum of squares is reduced
 // across the block instead of in index order: the terms are binary32 squares
-// whose f64 sum is exact whenever their exponents lie within 29 binades of the
-// largest, and otherwise differs only far below the binary32 rounding of the
-// mean, so the f32 result matches the reference's serial sum.
+// whose f64 sum is exact whenever their exponents lie within ~29 binades of the
+// largest; otherwise it differs from the serial sum by a few f64 ulps, which
+// changes the binary32 mean only when that lies within those ulps of a
+// binary32 rounding boundary (about 2^-27 per norm).
 __global__ void rmsnorm_quant_kernel(Batch b, const float* __restrict__ weight,
                                      uint32_t layer_ordinal, uint32_t domain) {
   __shared__ float y[kHidden];
