@@ -202,6 +202,18 @@ PB_API uint32_t pb_sample_batch_device(uint32_t *logits_device, uint64_t ld, uin
  * Scratch: the quantized x; allocated per call. */
 PB_API uint32_t pb_qmatvec_device(uint32_t wtype, const uint8_t *w_device, uint32_t rows, uint32_t cols,
                            const float *x_device, uint32_t batch, float *y_device, void *stream);
+/* The same operator without any device allocation (no counterpart in the
+ * reference): for callers that cannot allocate device memory on this path,
+ * e.g. hosts that own the GPU's memory budget through their own allocator,
+ * latency-critical loops, or fixed-arena integrations like promptboot's own
+ * firmware runtime.  Its scratch is one file-scope device array of 192 KiB
+ * held by each GPU that loads the library; batch is limited to 32 rows and
+ * cols to 4864 (PB_CAPACITY otherwise, see pb_last_error_string).  The first
+ * call on a device sets it up and should come before any stream capture; all
+ * calls share the array, so calls that overlap on the GPU race. */
+PB_API uint32_t pb_qmatvec_device_noalloc(uint32_t wtype, const uint8_t *w_device, uint32_t rows,
+                                          uint32_t cols, const float *x_device, uint32_t batch,
+                                          float *y_device, void *stream);
 /* Q8_0 staging in the reference's 34-byte block format for [rows][cols] f32. */
 PB_API uint32_t pb_quantize_q8_device(const float *x_device, uint32_t rows, uint32_t cols,
                                uint8_t *staging_device, void *stream);

@@ -22,6 +22,9 @@ uint32_t record_cuda_error(cudaError_t e, const char* what);
     if (pb_e_ != cudaSuccess) return ::pb::record_cuda_error(pb_e_, #call); \
   } while (0)
 
+// Sets the text returned by pb_last_error_string() for a non-CUDA failure.
+void set_last_error(const char* text);
+
 void sha256(const uint8_t* data, size_t len, uint8_t out[32]);
 
 // The 8 MiB inference RoPE table (tests/fixtures/inference/

@@ -10,6 +10,8 @@ namespace pb {
 
 static thread_local std::string g_last_error;
 
+void set_last_error(const char* text) { g_last_error = text; }
+
 uint32_t record_cuda_error(cudaError_t e, const char* what) {
   g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
   return PB_DEVICE;
