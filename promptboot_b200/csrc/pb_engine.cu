@@ -143,6 +143,8 @@ struct pb_engine {
   pb::SamplerRow* d_sampled = nullptr;
   unsigned long long* d_samp_status = nullptr;  // [kErrSteps][max_seqs]
   uint32_t* d_token_log = nullptr;              // [kErrSteps][max_seqs]
+  unsigned int* d_tc_status = nullptr;          // tensor-core pipeline timeout flag
+  unsigned int* h_tc_status = nullptr;
 
   // pinned host staging
   int *h_slots = nullptr, *h_positions = nullptr;
@@ -223,30 +225,38 @@ struct pb_engine {
       PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(T(10)), ord,
                                                  D_ATTN_NORM, stream));
       Epilogue ep{EPI_BIAS, q, kHidden, reinterpret_cast<const float*>(T(18)), err, ord, D_Q};
+      ep.tc_status = d_tc_status;
       PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(19), 896, 896, b, ep, stream));
       ep = {EPI_BIAS, k, 128, reinterpret_cast<const float*>(T(15)), err, ord, D_K};
+      ep.tc_status = d_tc_status;
       PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(16), 128, 896, b, ep, stream));
       ep = {EPI_BIAS, v, 128, reinterpret_cast<const float*>(T(20)), err, ord, D_V};
+      ep.tc_status = d_tc_status;
       PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(21), 128, 896, b, ep, stream));
       PB_LAUNCH(PB_KC_ROPE_KV, launch_rope_kv(b, layer, m->rope, stream));
       PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, stream));
       PB_LAUNCH(PB_KC_QUANT, launch_quant(b, attn, kHidden, kHidden, stream));
       ep = {EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_ATTN_OUTPUT};
+      ep.tc_status = d_tc_status;
       PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(17), 896, 896, b, ep, stream));
       PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(T(14)), ord,
                                                  D_FFN_NORM, stream));
       ep = {EPI_STORE, gate, kFfn, nullptr, err, ord, D_GATE};
+      ep.tc_status = d_tc_status;
       PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(12), 4864, 896, b, ep, stream));
       ep = {EPI_STORE, up, kFfn, nullptr, err, ord, D_UP};
+      ep.tc_status = d_tc_status;
       PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(13), 4864, 896, b, ep, stream));
       PB_LAUNCH(PB_KC_SWIGLU, launch_swiglu_quant(b, ord, stream));
       ep = {EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_DOWN};
+      ep.tc_status = d_tc_status;
       PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(11), 896, 4864, b, ep, stream));
     }
     if (want_logits) {
       PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(m->tensor(289)),
                                                  25, D_OUTPUT_NORM, stream));
       Epilogue ep{EPI_STORE, logits, (size_t)kVocab, nullptr, err, 25, D_LOGITS};
+      ep.tc_status = d_tc_status;
       PB_LAUNCH(PB_KC_LM_HEAD, launch_qgemv(W_Q8_0, m->tensor(290), kVocab, 896, b, ep, stream));
       PB_LAUNCH(PB_KC_ARGMAX, launch_argmax(logits, kVocab, rows, kVocab, d_greedy, d_greedy_bits,
                                             nullptr, stream));
@@ -266,6 +276,7 @@ struct pb_engine {
     enqueue_forward(rows, want_logits, d_err);
     PB_CUDA(cudaGetLastError());
     PB_CUDA(cudaMemcpyAsync(h_err, d_err, rows * 8, cudaMemcpyDeviceToHost, stream));
+    PB_CUDA(cudaMemcpyAsync(h_tc_status, d_tc_status, 4, cudaMemcpyDeviceToHost, stream));
     if (want_logits) {
       PB_CUDA(cudaMemcpyAsync(h_greedy, d_greedy, rows * 4, cudaMemcpyDeviceToHost, stream));
       PB_CUDA(cudaMemcpyAsync(h_greedy_bits, d_greedy_bits, rows * 4, cudaMemcpyDeviceToHost, stream));
@@ -273,6 +284,16 @@ struct pb_engine {
     }
     PB_CUDA(cudaStreamSynchronize(stream));
     prof_resolve();
+    return check_tc_status();
+  }
+
+  // A tensor-core pipeline wait that timed out (never expected) poisons the
+  // engine's results: report it as a device failure.
+  uint32_t check_tc_status() {
+    if (*h_tc_status) {
+      pb::set_last_error("tensor-core matvec pipeline timed out waiting for an MMA");
+      return PB_DEVICE;
+    }
     return PB_OK;
   }
 
@@ -490,6 +511,8 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   chk(dalloc(&e->d_sampled, S));
   chk(dalloc(&e->d_samp_status, S * pb_engine::kErrSteps));
   chk(dalloc(&e->d_token_log, S * pb_engine::kErrSteps));
+  chk(dalloc(&e->d_tc_status, 1));
+  chk(cudaMallocHost(&e->h_tc_status, 4));
   chk(cudaMallocHost(&e->h_slots, S * 4));
   chk(cudaMallocHost(&e->h_positions, S * 4));
   chk(cudaMallocHost(&e->h_tokens, S * 4));
@@ -499,6 +522,8 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   if (c == cudaSuccess) pb::init_kernel_attributes();
   if (c == cudaSuccess) c = cudaMemset(e->kv, 0, S * (size_t)max_context * 6144 * 4);
   if (c == cudaSuccess) c = cudaMemset(e->history, 0, S * (size_t)max_context * 4);
+  if (c == cudaSuccess) c = cudaMemset(e->d_tc_status, 0, 4);
+  if (c == cudaSuccess) *e->h_tc_status = 0;
   if (c != cudaSuccess) {
     pb::record_cuda_error(c, "pb_engine_create");
     if (err) *err = make_error(PB_DEVICE, 1, NO_LAYER, 0, NO_TENSOR, 0, (uint64_t)c, K_BYTES, 1);
@@ -517,9 +542,10 @@ void pb_engine_destroy(pb_engine* e) {
                  e->logits, e->scores, e->aq, e->ad, e->asum, e->d_slots, e->d_positions,
                  e->d_tokens, e->d_err, e->d_greedy, e->d_greedy_bits, e->d_states,
                  e->d_hist_offset, e->d_hist_len, e->d_sampled, e->d_samp_status,
-                 e->d_token_log};
+                 e->d_token_log, e->d_tc_status};
   for (void* p : dev) if (p) cudaFree(p);
-  void* host[] = {e->h_slots, e->h_positions, e->h_tokens, e->h_err, e->h_greedy, e->h_greedy_bits};
+  void* host[] = {e->h_slots, e->h_positions, e->h_tokens, e->h_err, e->h_greedy, e->h_greedy_bits,
+                  e->h_tc_status};
   for (void* p : host) if (p) cudaFreeHost(p);
   for (cudaEvent_t ev : e->prof_events) cudaEventDestroy(ev);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -836,8 +862,10 @@ uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
     PB_CUDA(cudaMemcpyAsync(toks.data(), e->d_token_log, (size_t)chunk * n * 4, cudaMemcpyDeviceToHost, e->stream));
     PB_CUDA(cudaMemcpyAsync(e->h_greedy, e->d_greedy, n * 4, cudaMemcpyDeviceToHost, e->stream));
     PB_CUDA(cudaMemcpyAsync(e->h_greedy_bits, e->d_greedy_bits, n * 4, cudaMemcpyDeviceToHost, e->stream));
+    PB_CUDA(cudaMemcpy(e->h_tc_status, e->d_tc_status, 4, cudaMemcpyDeviceToHost));
     PB_CUDA(cudaStreamSynchronize(e->stream));
     e->prof_resolve();
+    if (e->check_tc_status()) return PB_DEVICE;
     for (uint32_t t = 0; t < chunk; ++t)
       for (uint32_t i = 0; i < n; ++i) {
         Slot& s = e->slots[seqs[i]];

@@ -49,6 +49,9 @@ struct Epilogue {
   unsigned long long* err;
   uint32_t layer_ordinal;
   uint32_t domain;
+  // Device word the tensor-core path sets on a pipeline timeout; when null the
+  // CUDA-core matvec serves every batch size.
+  unsigned int* tc_status = nullptr;
 };
 
 enum WeightType : int { W_Q4_0 = 2, W_Q8_0 = 3 };
@@ -60,6 +63,10 @@ void launch_rmsnorm_quant(const Batch& b, const float* weight, uint32_t layer_or
 void launch_quant(const Batch& b, const float* x, size_t ld, int columns, cudaStream_t s);
 void launch_qgemv(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
                   const Epilogue& ep, cudaStream_t s);
+// tcgen05 kind::i8 path (pb_gemm_tc.cu) for batches above 8 rows.
+bool qgemm_tc_supported(int rows, int batch);
+void launch_qgemm_tc(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
+                     const Epilogue& ep, unsigned int* status, cudaStream_t s);
 void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s);
 void launch_attention(const Batch& b, int layer, cudaStream_t s);
 void launch_swiglu_quant(const Batch& b, uint32_t layer_ordinal, cudaStream_t s);

@@ -104,6 +104,7 @@ struct OpScratch {
   unsigned long long* err = nullptr;
   int* slots = nullptr;
   int* positions = nullptr;
+  unsigned int* tc_status = nullptr;
   cudaStream_t s;
   explicit OpScratch(cudaStream_t st) : s(st) {}
   cudaError_t alloc(uint32_t rows) {
@@ -113,12 +114,14 @@ struct OpScratch {
     if (!e) e = cudaMallocAsync(&err, (size_t)rows * 8, s);
     if (!e) e = cudaMallocAsync(&slots, (size_t)rows * 4, s);
     if (!e) e = cudaMallocAsync(&positions, (size_t)rows * 4, s);
+    if (!e) e = cudaMallocAsync(&tc_status, 4, s);
+    if (!e) e = cudaMemsetAsync(tc_status, 0, 4, s);
     if (!e) e = cudaMemsetAsync(err, 0xff, (size_t)rows * 8, s);
     if (!e) iota_kernel<<<(rows + 127) / 128, 128, 0, s>>>(slots, (int)rows);
     return e;
   }
   ~OpScratch() {
-    void* p[] = {aq, ad, asum, err, slots, positions};
+    void* p[] = {aq, ad, asum, err, slots, positions, tc_status};
     for (void* x : p) if (x) cudaFreeAsync(x, s);
   }
   pb::Batch batch(uint32_t rows) const {
@@ -232,8 +235,16 @@ uint32_t pb_qmatvec_device(uint32_t wtype, const uint8_t* w, uint32_t rows, uint
   pb::Batch b = scr.batch(batch);
   pb::launch_quant(b, x, cols, (int)cols, s);
   pb::Epilogue ep{pb::EPI_STORE, y, rows, nullptr, scr.err, 0, 0};
+  ep.tc_status = scr.tc_status;
   pb::launch_qgemv((int)wtype, w, (int)rows, (int)cols, b, ep, s);
   PB_CUDA(cudaGetLastError());
+  unsigned int status = 0;
+  PB_CUDA(cudaMemcpyAsync(&status, scr.tc_status, 4, cudaMemcpyDeviceToHost, s));
+  PB_CUDA(cudaStreamSynchronize(s));
+  if (status) {
+    pb::set_last_error("tensor-core matvec pipeline timed out waiting for an MMA");
+    return PB_DEVICE;
+  }
   return PB_OK;
 }
 

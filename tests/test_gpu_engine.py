@@ -96,6 +96,25 @@ def test_batched_device_generation_matches_oracle(model_view, model_image):
     e.close()
 
 
+def test_tensor_core_batch_generation_matches_oracle(model_view, model_image):
+    """12 sequences: every layer matvec and the lm_head run on the tcgen05 path."""
+    n = 12
+    e = api.InferenceEngine(model_view, max_seqs=n, max_context=32)
+    prompts = np.stack([prompt(5, seed=100 + s) for s in range(n)])
+    status, steps, errs = e.prefill_batch(list(range(n)), prompts, 16)
+    assert status == 0
+    rows = [e.logits(i) for i in range(n)]
+    for i in (0, n - 1):
+        ref, _ = oracle_prefill_logits(model_image, prompts[i])
+        assert np.array_equal(rows[i], ref.view(np.uint32)), i
+    states = [api.SamplingState(s) for s in range(n)]
+    status, out, errs = e.generate(list(range(n)), states, 3)
+    assert status == 0
+    ref = oracle.generate_many(model_image, prompts, 4, np.arange(n), 32, oracle.cpu_cores())
+    assert np.array_equal(out, ref[:, :3].T)
+    e.close()
+
+
 def test_engine_sample_matches_host_sampler(model_view):
     e = api.InferenceEngine(model_view, max_seqs=2, max_context=64)
     prompts = np.stack([prompt(4, seed=20), prompt(4, seed=21)])

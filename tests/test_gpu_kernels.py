@@ -199,8 +199,10 @@ def test_matvec_dot_fixture():
 
 @pytest.mark.parametrize("wtype,rows,cols", [(2, 896, 896), (2, 128, 896), (2, 4864, 896),
                                              (2, 896, 4864), (3, 151936, 896)])
-@pytest.mark.parametrize("batch", [1, 8, 9])
+@pytest.mark.parametrize("batch", [1, 8, 9, 64, 256])
 def test_matvec_shapes_match_oracle(wtype, rows, cols, batch):
+    """B <= 8 runs the CUDA-core matvec, B > 8 the tcgen05 kind::i8 path (tile
+    widths 16/32/64 chosen by grid size); both must equal the oracle bit for bit."""
     lib = _lib.load()
     rng = np.random.default_rng(rows * 7 + cols + batch)
     w = _q4_weights(rng, rows, cols) if wtype == 2 else _q8_weights(rng, rows, cols)
@@ -213,4 +215,20 @@ def test_matvec_shapes_match_oracle(wtype, rows, cols, batch):
     for b in check_rows:
         st = oracle.prepare_q8(x[b])
         ref = oracle.q4_matvec(w, st, rows, cols) if wtype == 2 else oracle.q8_matvec(w, st, rows, cols)
+        assert np.array_equal(u32(got[b]), u32(ref)), b
+
+
+def test_tensor_core_widest_tile_matches_oracle():
+    """4864 x 896 Q4_0 at 512 rows selects the 64-sequence tile."""
+    lib = _lib.load()
+    rng = np.random.default_rng(512)
+    rows, cols, batch = 4864, 896, 512
+    w = _q4_weights(rng, rows, cols)
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    y = torch.zeros((batch, rows), dtype=torch.float32, device="cuda")
+    assert lib.pb_qmatvec_device(2, ptr(dev(w)), rows, cols, ptr(dev(x)), batch, ptr(y), None) == 0
+    sync()
+    got = host(y)
+    for b in (0, 63, 64, 300, 511):
+        ref = oracle.q4_matvec(w, oracle.prepare_q8(x[b]), rows, cols)
         assert np.array_equal(u32(got[b]), u32(ref)), b
