@@ -17,8 +17,12 @@
 // Shared-memory tiles use the canonical no-swizzle K-major layout: 8-row x
 // 16-byte core matrices, the two 16-byte K halves of an 8-row group adjacent
 // (leading byte offset 128), groups 256 bytes apart (stride byte offset 256).
-// Every mbarrier wait is bounded; a timeout sets *status, stops issuing, waits
-// (bounded) for work in flight, frees TMEM and returns.
+// Operands stream in through a 4-stage cp.async ring of 4-block chunks: raw
+// weight bytes (8-byte granules; 18- and 34-byte blocks are only 2-byte
+// aligned) are unpacked by the threads into the canonical A tile, while the
+// activation rows are scattered by 16-byte cp.async straight into the canonical
+// B layout.  Every mbarrier wait is bounded; a timeout sets *status, stops
+// issuing, waits (bounded) for work in flight, frees TMEM and returns.
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
 
@@ -111,40 +115,59 @@ __device__ __forceinline__ int tile_off(int row, int half) {
 constexpr int kM = 128;
 constexpr int kThreads = 128;
 
-constexpr int kStages = 3;  // smem stages (A/B tiles + scales); TMEM has 2 buffers
+constexpr int kKC = 4;    // Q-blocks per cp.async chunk
+constexpr int kRS = 4;    // chunk ring stages
+constexpr int kAbuf = 3;  // canonical A tiles (MMA operands)
 
-template <int NT>
-struct TcSmem {
-  static constexpr int kA = kM * 32;     // A tile bytes per stage
-  static constexpr int kB = NT * 32;     // B tile bytes per stage
-  static constexpr int kStage = kA + kB;
-  static constexpr int kScaleOff = kStages * kStage;                 // dA [kStages][NT] f32
-  static constexpr int kCOff = kScaleOff + kStages * NT * 4;         // C  [kStages][NT] i32
-  static constexpr int kMiscOff = kCOff + kStages * NT * 4;          // 2 mbarriers + slot
+template <int BPB, int NT>
+struct TcLayout {
+  static constexpr int kRowRaw = ((kKC * BPB + 15) / 16) * 16;  // 80 (Q4_0) / 144 (Q8_0)
+  static constexpr int kARaw = kM * kRowRaw;
+  static constexpr int kBTile = NT * 32;
+  static constexpr int kBRaw = kKC * kBTile;
+  static constexpr int kScale = NT * kKC * 4;
+  static constexpr int kDaOff = kARaw + kBRaw;
+  static constexpr int kCOff = kDaOff + kScale;
+  static constexpr int kStage = kCOff + kScale;
+  static constexpr int kAcanOff = kRS * kStage;
+  static constexpr int kMiscOff = kAcanOff + kAbuf * kM * 32;
   static constexpr int kBytes = kMiscOff + 64;
 };
 
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// One 18- or 34-byte block at a 2-byte aligned address: binary16 scale bits and
+// the 16 / 32 quant bytes as little-endian words, reading exactly its bytes.
 template <int BPB>
-__device__ __forceinline__ void load_weight_block(const uint8_t* __restrict__ w, size_t off,
-                                                  uint32_t& scale_bits, uint32_t (&q)[8]) {
-  // off is even; read exactly the block's bytes with 2- and 4-byte aligned loads.
-  const uint8_t* p = w + off;
-  if ((off & 3) == 0) {
+__device__ __forceinline__ void read_block(const uint8_t* p, uint32_t& scale_bits, uint32_t (&q)[8]) {
+  constexpr int nfull = BPB == 18 ? 4 : 8;
+  if ((smem_u32(p) & 3) == 0) {
     const uint32_t* p4 = reinterpret_cast<const uint32_t*>(p);
-    uint32_t words[BPB == 18 ? 5 : 9];
-    constexpr int nfull = BPB == 18 ? 4 : 8;
+    uint32_t words[nfull + 1];
 #pragma unroll
-    for (int i = 0; i < nfull; ++i) words[i] = __ldg(p4 + i);
-    words[nfull] = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(p + 4 * nfull));
+    for (int i = 0; i < nfull; ++i) words[i] = p4[i];
+    words[nfull] = *reinterpret_cast<const uint16_t*>(p + 4 * nfull);
     scale_bits = words[0] & 0xffffu;
 #pragma unroll
     for (int i = 0; i < nfull; ++i) q[i] = __funnelshift_r(words[i], words[i + 1], 16);
   } else {
-    scale_bits = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(p));
+    scale_bits = *reinterpret_cast<const uint16_t*>(p);
     const uint32_t* p4 = reinterpret_cast<const uint32_t*>(p + 2);
-    constexpr int nfull = BPB == 18 ? 4 : 8;
 #pragma unroll
-    for (int i = 0; i < nfull; ++i) q[i] = __ldg(p4 + i);
+    for (int i = 0; i < nfull; ++i) q[i] = p4[i];
   }
 }
 
@@ -152,10 +175,8 @@ template <int BPB, int NT>
 __global__ void __launch_bounds__(kThreads)
 qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilogue ep,
                 unsigned int* status) {
-  using L = TcSmem<NT>;
+  using L = TcLayout<BPB, NT>;
   extern __shared__ __align__(1024) uint8_t smem[];
-  float* dA_s = reinterpret_cast<float*>(smem + L::kScaleOff);
-  int* C_s = reinterpret_cast<int*>(smem + L::kCOff);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + L::kMiscOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff + 16);
 
@@ -168,6 +189,7 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
   const int row = blockIdx.y * kM + tid;
   const int nseq = min(NT, b.rows - seq0);
   const size_t row_bytes = (size_t)nb * BPB;
+  const int nchunks = nb / kKC;
 
   if (warp == 0) tmem_alloc(tmem_slot, kCols);
   if (tid == 0) {
@@ -180,113 +202,143 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
   tc_after_sync();
   const uint32_t tmem_base = *tmem_slot;
 
-  float acc[NT];
+  // Stream chunk c (blocks 4c..4c+3) into ring stage c % kRS; always commits a
+  // group so that cp.async.wait_group counts stay uniform.
+  auto issue_chunk = [&](int c) {
+    if (c < nchunks) {
+      uint8_t* st = smem + (c % kRS) * L::kStage;
+      const int blk0 = c * kKC;
+      const uint8_t* src = w + (size_t)row * row_bytes + (size_t)blk0 * BPB;
+      uint8_t* dst = st + tid * L::kRowRaw;
 #pragma unroll
-  for (int s = 0; s < NT; ++s) acc[s] = 0.0f;
-
-  // Stage one Q-block: A rows (one per thread), B rows (threads < NT), scales.
-  auto load_stage = [&](int st, int blk, float& dW, float& negMdW) {
-    uint32_t sb, q[8];
-    load_weight_block<BPB>(w, (size_t)row * row_bytes + (size_t)blk * BPB, sb, q);
-    dW = half_to_f32((uint16_t)sb);
-    negMdW = -__fmul_rn(12582912.0f, dW);
-    uint8_t* A = smem + st * L::kStage;
-    uint4 h0, h1;
-    if (BPB == 18) {
-      h0 = make_uint4(q[0] & 0x0f0f0f0fu, q[1] & 0x0f0f0f0fu, q[2] & 0x0f0f0f0fu, q[3] & 0x0f0f0f0fu);
-      h1 = make_uint4((q[0] >> 4) & 0x0f0f0f0fu, (q[1] >> 4) & 0x0f0f0f0fu,
-                      (q[2] >> 4) & 0x0f0f0f0fu, (q[3] >> 4) & 0x0f0f0f0fu);
-    } else {
-      h0 = make_uint4(q[0], q[1], q[2], q[3]);
-      h1 = make_uint4(q[4], q[5], q[6], q[7]);
-    }
-    *reinterpret_cast<uint4*>(A + tile_off(tid, 0)) = h0;
-    *reinterpret_cast<uint4*>(A + tile_off(tid, 1)) = h1;
-    if (tid < NT) {
-      uint8_t* B = A + L::kA;
-      uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0;
-      float da = 0.0f;
-      int c = 0x4B400000;
-      if (tid < nseq) {
-        const size_t srow = (size_t)(seq0 + tid);
-        const uint4* ap = reinterpret_cast<const uint4*>(b.aq + srow * kActStride + blk * 32);
-        a0 = ap[0];
-        a1 = ap[1];
-        da = b.ad[srow * kActBlocks + blk];
-        c = 0x4B400000 - 8 * b.asum[srow * kActBlocks + blk];
+      for (int g = 0; g < kKC * BPB / 8; ++g) cp_async8(dst + 8 * g, src + 8 * g);
+      if (tid < NT) {
+        const bool valid = tid < nseq;
+        const size_t srow = valid ? (size_t)(seq0 + tid) : 0;
+        const int8_t* a = b.aq + srow * kActStride + (size_t)blk0 * 32;
+#pragma unroll
+        for (int j = 0; j < kKC; ++j) {
+          cp_async16(st + L::kARaw + j * L::kBTile + tile_off(tid, 0), a + j * 32, valid);
+          cp_async16(st + L::kARaw + j * L::kBTile + tile_off(tid, 1), a + j * 32 + 16, valid);
+        }
+        cp_async16(st + L::kDaOff + tid * kKC * 4, b.ad + srow * kActBlocks + blk0, valid);
+        cp_async16(st + L::kCOff + tid * kKC * 4, b.asum + srow * kActBlocks + blk0, valid);
       }
-      *reinterpret_cast<uint4*>(B + tile_off(tid, 0)) = a0;
-      *reinterpret_cast<uint4*>(B + tile_off(tid, 1)) = a1;
-      dA_s[st * NT + tid] = da;
-      C_s[st * NT + tid] = c;
     }
-    fence_async_shared();  // generic-proxy smem writes -> visible to the tensor core
+    cp_async_commit();
   };
-  auto issue = [&](int blk) {
-    uint8_t* A = smem + (blk % kStages) * L::kStage;
-    mma_i8(tmem_base + (uint32_t)((blk & 1) * NT), smem_desc(A), smem_desc(A + L::kA), kIdesc);
+  auto issue_mma = [&](int blk) {
+    const uint8_t* A = smem + L::kAcanOff + (blk % kAbuf) * (kM * 32);
+    const uint8_t* B = smem + ((blk / kKC) % kRS) * L::kStage + L::kARaw + (blk % kKC) * L::kBTile;
+    mma_i8(tmem_base + (uint32_t)((blk & 1) * NT), smem_desc(A), smem_desc(B), kIdesc);
     mma_commit(&mbar[blk & 1]);
   };
 
-  // Pipeline: in iteration k the CTA stages block k+1 (smem stage (k+1)%3, last
-  // read by MMA k-2, already complete), then thread 0 issues MMA k+1 into TMEM
-  // buffer (k+1)&1 (drained in iteration k-1), while all warps wait for MMA k
-  // and drain buffer k&1.  Barrier votes keep every exit block-uniform.
-  float dW_cur, negMdW_cur, dW_next = 0.0f, negMdW_next = 0.0f;
+  float acc[NT];
+#pragma unroll
+  for (int s = 0; s < NT; ++s) acc[s] = 0.0f;
+  float dW_prev = 0.0f, negMdW_prev = 0.0f;
   uint32_t phase[2] = {0, 0};
-  int pending[2] = {0, 0};  // MMAs committed and not yet waited for, per buffer (thread 0)
-  load_stage(0, 0, dW_cur, negMdW_cur);
-  tc_before_sync();
-  __syncthreads();
-  tc_after_sync();
-  if (tid == 0) { issue(0); pending[0] = 1; }
-  int timed_out = 0;
-  for (int blk = 0; blk < nb; ++blk) {
-    const int buf = blk & 1;
-    if (blk + 1 < nb) load_stage((blk + 1) % kStages, blk + 1, dW_next, negMdW_next);
-    tc_before_sync();
-    const int stop = __syncthreads_or(timed_out);
-    tc_after_sync();
-    if (stop) break;
-    if (tid == 0 && blk + 1 < nb) { issue(blk + 1); pending[buf ^ 1] = 1; }
-    if (!mbar_wait_bounded(&mbar[buf], phase[buf])) {
-      timed_out = 1;
-      continue;  // the vote at the top of the next iteration stops everyone
-    }
-    if (tid == 0) pending[buf] = 0;
-    phase[buf] ^= 1u;
-    const int st = blk % kStages;
-    const float* dA = dA_s + st * NT;
-    const int* C = C_s + st * NT;
-    const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * NT);
+  int pending[2] = {0, 0};  // thread 0: committed MMAs not yet waited for
+
+  // Drains block `blk` (MMA already waited for) from TMEM into the accumulators.
+  auto epilogue = [&](int blk, float dW, float negMdW) {
+    const uint8_t* st = smem + ((blk / kKC) % kRS) * L::kStage;
+    const float* dA = reinterpret_cast<const float*>(st + L::kDaOff);
+    const int* C = reinterpret_cast<const int*>(st + L::kCOff);
+    const int j = blk % kKC;
+    const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)((blk & 1) * NT);
 #pragma unroll
     for (int c0 = 0; c0 < NT; c0 += 16) {
       uint32_t v[16];
       tmem_ld16(taddr + c0, v);
       tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int s = c0 + j;
+      for (int jj = 0; jj < 16; ++jj) {
+        const int s = c0 + jj;
+        const float da = dA[s * kKC + j];
         float t;
         if (BPB == 18) {
-          const float x = __int_as_float((int)v[j] + C[s]);
-          t = __fmul_rn(__fmaf_rn(x, dW_cur, negMdW_cur), dA[s]);
+          const float x = __int_as_float((int)v[jj] + C[s * kKC + j]);
+          t = __fmul_rn(__fmaf_rn(x, dW, negMdW), da);
         } else {
-          const float f = __fsub_rn(__int_as_float((int)v[j] + 0x4B400000), 12582912.0f);
-          t = __fmul_rn(f, __fmul_rn(dW_cur, dA[s]));
+          const float f = __fsub_rn(__int_as_float((int)v[jj] + 0x4B400000), 12582912.0f);
+          t = __fmul_rn(f, __fmul_rn(dW, da));
         }
         acc[s] = __fadd_rn(acc[s], t);
       }
     }
-    dW_cur = dW_next;
-    negMdW_cur = negMdW_next;
+  };
+
+  for (int c = 0; c < kRS; ++c) issue_chunk(c);
+  int timed_out = 0;
+  int blk = 0;
+  for (; blk < nb; ++blk) {
+    const int c = blk / kKC, j = blk % kKC;
+    uint8_t* st = smem + (c % kRS) * L::kStage;
+    if (j == 0) {
+      cp_async_wait<kRS - 2>();
+      __syncthreads();
+      if (BPB == 18 && tid < NT) {
+        int* C = reinterpret_cast<int*>(st + L::kCOff);
+#pragma unroll
+        for (int k = 0; k < kKC; ++k) C[tid * kKC + k] = 0x4B400000 - 8 * C[tid * kKC + k];
+      }
+    }
+    // unpack this thread's row of block blk into canonical A tile blk % kAbuf
+    uint32_t sb, q[8];
+    read_block<BPB>(st + tid * L::kRowRaw + j * BPB, sb, q);
+    const float dW = half_to_f32((uint16_t)sb);
+    const float negMdW = -__fmul_rn(12582912.0f, dW);
+    uint8_t* A = smem + L::kAcanOff + (blk % kAbuf) * (kM * 32);
+    if (BPB == 18) {
+      *reinterpret_cast<uint4*>(A + tile_off(tid, 0)) =
+          make_uint4(q[0] & 0x0f0f0f0fu, q[1] & 0x0f0f0f0fu, q[2] & 0x0f0f0f0fu, q[3] & 0x0f0f0f0fu);
+      *reinterpret_cast<uint4*>(A + tile_off(tid, 1)) =
+          make_uint4((q[0] >> 4) & 0x0f0f0f0fu, (q[1] >> 4) & 0x0f0f0f0fu,
+                     (q[2] >> 4) & 0x0f0f0f0fu, (q[3] >> 4) & 0x0f0f0f0fu);
+    } else {
+      *reinterpret_cast<uint4*>(A + tile_off(tid, 0)) = make_uint4(q[0], q[1], q[2], q[3]);
+      *reinterpret_cast<uint4*>(A + tile_off(tid, 1)) = make_uint4(q[4], q[5], q[6], q[7]);
+    }
+    fence_async_shared();
+    tc_before_sync();
+    const int stop = __syncthreads_or(timed_out);
+    tc_after_sync();
+    if (stop) break;
+    // every thread has drained block blk-2 (the last block of chunk c-1 when
+    // j == 1), so that chunk's ring stage can be refilled
+    if (j == 1 && c >= 1) issue_chunk(c - 1 + kRS);
+    if (tid == 0) { issue_mma(blk); pending[blk & 1] = 1; }
+    if (blk >= 1) {
+      const int pb = blk - 1;
+      if (!mbar_wait_bounded(&mbar[pb & 1], phase[pb & 1])) {
+        timed_out = 1;
+      } else {
+        phase[pb & 1] ^= 1u;
+        if (tid == 0) pending[pb & 1] = 0;
+        epilogue(pb, dW_prev, negMdW_prev);
+      }
+    }
+    dW_prev = dW;
+    negMdW_prev = negMdW;
   }
+  if (!timed_out && blk == nb) {
+    const int pb = nb - 1;
+    if (!mbar_wait_bounded(&mbar[pb & 1], phase[pb & 1])) {
+      timed_out = 1;
+    } else {
+      phase[pb & 1] ^= 1u;
+      if (tid == 0) pending[pb & 1] = 0;
+      epilogue(pb, dW_prev, negMdW_prev);
+    }
+  }
+  cp_async_wait_all();
   tc_before_sync();
   const int aborted = __syncthreads_or(timed_out);
   tc_after_sync();
   if (aborted && tid == 0) {
     atomicOr(status, 1u);
-    // Wait (bounded) for MMAs still in flight before their TMEM is released.
     for (int k = 0; k < 2; ++k)
       if (pending[k]) mbar_wait_bounded(&mbar[k], phase[k]);
   }
@@ -314,13 +366,21 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
 template <int BPB, int NT>
 void launch_tc(const uint8_t* w, int rows, int nb, const Batch& b, const Epilogue& ep,
                unsigned int* status, cudaStream_t s) {
+  static bool configured = false;  // per process; the attribute is per function
+  if (!configured) {
+    cudaFuncSetAttribute(qgemm_tc_kernel<BPB, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         TcLayout<BPB, NT>::kBytes);
+    configured = true;
+  }
   dim3 grid((b.rows + NT - 1) / NT, rows / kM);
-  qgemm_tc_kernel<BPB, NT><<<grid, kThreads, TcSmem<NT>::kBytes, s>>>(w, rows, nb, b, ep, status);
+  qgemm_tc_kernel<BPB, NT><<<grid, kThreads, TcLayout<BPB, NT>::kBytes, s>>>(w, rows, nb, b, ep, status);
 }
 
 }  // namespace
 
-bool qgemm_tc_supported(int rows, int batch) { return rows % kM == 0 && batch > 8; }
+bool qgemm_tc_supported(int rows, int batch, int columns) {
+  return rows % kM == 0 && batch > 8 && (columns / 32) % kKC == 0;
+}
 
 // Picks the sequence tile so that the grid covers the 148 SMs; the weight tile
 // is the slow grid dimension so the CTAs sharing it run together (one HBM read).

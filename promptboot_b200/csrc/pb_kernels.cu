@@ -265,7 +265,7 @@ static size_t qgemv_smem(int nb) {
 void launch_qgemv(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
                   const Epilogue& ep, cudaStream_t s) {
   const int nb = columns / 32;
-  if (ep.tc_status && qgemm_tc_supported(rows, b.rows)) {
+  if (ep.tc_status && qgemm_tc_supported(rows, b.rows, columns)) {
     launch_qgemm_tc(wtype, w, rows, columns, b, ep, ep.tc_status, s);
     return;
   }

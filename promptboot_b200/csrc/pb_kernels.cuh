@@ -64,7 +64,7 @@ void launch_quant(const Batch& b, const float* x, size_t ld, int columns, cudaSt
 void launch_qgemv(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
                   const Epilogue& ep, cudaStream_t s);
 // tcgen05 kind::i8 path (pb_gemm_tc.cu) for batches above 8 rows.
-bool qgemm_tc_supported(int rows, int batch);
+bool qgemm_tc_supported(int rows, int batch, int columns);
 void launch_qgemm_tc(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
                      const Epilogue& ep, unsigned int* status, cudaStream_t s);
 void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s);
