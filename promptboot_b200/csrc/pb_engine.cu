@@ -153,6 +153,7 @@ struct pb_engine {
   uint32_t *h_greedy = nullptr, *h_greedy_bits = nullptr;
 
   uint32_t last_rows = 0;  // rows of the last forward (logits rows valid)
+  int max_span = 4;        // largest softmax span of the step being enqueued
   static constexpr uint32_t kErrSteps = 256;
 
   // Launch accounting and optional per-class CUDA-event timing on `stream`.
@@ -234,7 +235,7 @@ struct pb_engine {
       ep.tc_status = d_tc_status;
       PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(21), 128, 896, b, ep, stream));
       PB_LAUNCH(PB_KC_ROPE_KV, launch_rope_kv(b, layer, m->rope, stream));
-      PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, stream));
+      PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, max_span, stream));
       PB_LAUNCH(PB_KC_QUANT, launch_quant(b, attn, kHidden, kHidden, stream));
       ep = {EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_ATTN_OUTPUT};
       ep.tc_status = d_tc_status;
@@ -273,6 +274,8 @@ struct pb_engine {
     PB_CUDA(cudaMemcpyAsync(d_slots, h_slots, rows * 4, cudaMemcpyHostToDevice, stream));
     PB_CUDA(cudaMemcpyAsync(d_tokens, h_tokens, rows * 4, cudaMemcpyHostToDevice, stream));
     PB_CUDA(cudaMemcpyAsync(d_positions, h_positions, rows * 4, cudaMemcpyHostToDevice, stream));
+    max_span = 4;
+    for (uint32_t i = 0; i < rows; ++i) max_span = std::max(max_span, (pos[i] + 4) & ~3);
     enqueue_forward(rows, want_logits, d_err);
     PB_CUDA(cudaGetLastError());
     PB_CUDA(cudaMemcpyAsync(h_err, d_err, rows * 8, cudaMemcpyDeviceToHost, stream));
@@ -850,6 +853,10 @@ uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
           e->d_sampled, e->d_samp_status + (size_t)t * n, (int)n);
       advance_kernel<<<blocks, threads, 0, e->stream>>>(
           e->d_sampled, e->d_tokens, e->d_positions, e->d_token_log + (size_t)t * n, (int)n);
+      e->max_span = 4;
+      for (uint32_t i = 0; i < n; ++i)
+        e->max_span = std::max(e->max_span,
+                               (int)((e->slots[seqs[i]].position + done + t + 4) & ~3u));
       e->enqueue_forward(n, true, e->d_err + (size_t)t * n);
       increment_kernel<<<blocks, threads, 0, e->stream>>>(e->d_positions, (int)n);
       e->launches += 4;

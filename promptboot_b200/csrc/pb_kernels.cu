@@ -390,7 +390,11 @@ __global__ void attention_kernel(Batch b, int layer) {
   }
 }
 
-void launch_attention(const Batch& b, int layer, cudaStream_t s) {
+void launch_attention(const Batch& b, int layer, int max_span, cudaStream_t s) {
+  if (max_span <= kAttnMaxPositions) {
+    launch_attention_grouped(b, layer, (max_span + 3) & ~3, s);
+    return;
+  }
   attention_kernel<<<b.rows * kQHeads, 256, 0, s>>>(b, layer);
 }
 

@@ -37,7 +37,12 @@ struct Batch {
   float* norm_out = nullptr;     // optional [B][896] RMSNorm output (operator API)
   float* product_out = nullptr;  // optional [B][4864] SwiGLU output (operator API)
   int span_min = 0;              // minimum softmax span (operator API; 0 = natural)
+  float* probs_out = nullptr;    // optional [B][14][score_stride] final probabilities
 };
+
+// Longest softmax span the shared-memory attention path holds; longer contexts
+// use the per-query-head kernel with global scores.
+constexpr int kAttnMaxPositions = 2048;
 
 enum EpiMode : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
 
@@ -68,7 +73,9 @@ bool qgemm_tc_supported(int rows, int batch, int columns);
 void launch_qgemm_tc(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
                      const Epilogue& ep, unsigned int* status, cudaStream_t s);
 void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s);
-void launch_attention(const Batch& b, int layer, cudaStream_t s);
+// max_span: the largest softmax span of the batch, (position + 4) & ~3 (or span_min).
+void launch_attention(const Batch& b, int layer, int max_span, cudaStream_t s);
+void launch_attention_grouped(const Batch& b, int layer, int span_cap, cudaStream_t s);
 void launch_swiglu_quant(const Batch& b, uint32_t layer_ordinal, cudaStream_t s);
 void launch_argmax(const float* logits, size_t ld, int rows, int words, uint32_t* ids,
                    uint32_t* bits, unsigned long long* first_nonfinite, cudaStream_t s);

@@ -331,7 +331,8 @@ uint32_t pb_attention_device(const float* q, const float* kv, uint32_t capacity,
   pb::Batch b = scr.batch(rows);
   b.q = const_cast<float*>(q); b.kv = const_cast<float*>(kv); b.capacity = capacity;
   b.attn = out; b.scores = sc; b.score_stride = span_max; b.span_min = (int)span;
-  pb::launch_attention(b, (int)layer, s);
+  b.probs_out = scores;
+  pb::launch_attention(b, (int)layer, (int)span_max, s);
   PB_CUDA(cudaGetLastError());
   if (!scores) PB_CUDA(cudaFreeAsync(sc, s));
   return PB_OK;

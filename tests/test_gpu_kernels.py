@@ -129,12 +129,15 @@ def test_attention_matches_fixtures(current, span, fixture, rot):
     assert last_head.tobytes() == (GOLDEN / f"scores-{fixture}.bin").read_bytes()
 
 
-@pytest.mark.parametrize("positions", [[0, 1, 2], [3, 4, 5], [29, 255, 256], [511, 512, 600]])
-def test_attention_random_kv_matches_oracle(positions):
-    """Edge spans (1..N positions, masked tails) and the reference's denormal /
-    signed-zero query words (tests.rs:699-706)."""
+@pytest.mark.parametrize("positions,cap", [([0, 1, 2], 1024), ([3, 4, 5], 1024),
+                                          ([29, 255, 256], 1024), ([511, 512, 600], 1024),
+                                          ([63, 64, 65], 1024), ([1023, 2046, 2047], 2048),
+                                          ([2048, 2100, 1], 2560)])
+def test_attention_random_kv_matches_oracle(positions, cap):
+    """Edge spans (1..N positions, masked tails, tile boundaries at 64), the
+    shared-memory path up to 2048 positions and the global-scores path beyond,
+    and the reference's denormal / signed-zero query words (tests.rs:699-706)."""
     lib = _lib.load()
-    cap = 1024
     rows = len(positions)
     rng = np.random.default_rng(sum(positions))
     kv = np.zeros(rows * 24 * 4 * cap * 64, dtype=np.float32)
