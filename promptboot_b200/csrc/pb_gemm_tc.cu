@@ -113,11 +113,10 @@ __device__ __forceinline__ int tile_off(int row, int half) {
 }
 
 constexpr int kM = 128;
-constexpr int kThreads = 128;
 
-constexpr int kKC = 4;    // Q-blocks per cp.async chunk
-constexpr int kRS = 4;    // chunk ring stages
-constexpr int kAbuf = 3;  // canonical A tiles (MMA operands)
+constexpr int kKC = 4;     // Q-blocks per cp.async chunk = MMAs per commit group
+constexpr int kRS = 4;     // chunk ring stages
+constexpr int kWarps = 8;  // two warps per TMEM lane quarter, each draining half the columns
 
 template <int BPB, int NT>
 struct TcLayout {
@@ -129,9 +128,11 @@ struct TcLayout {
   static constexpr int kDaOff = kARaw + kBRaw;
   static constexpr int kCOff = kDaOff + kScale;
   static constexpr int kStage = kCOff + kScale;
-  static constexpr int kAcanOff = kRS * kStage;
-  static constexpr int kMiscOff = kAcanOff + kAbuf * kM * 32;
+  static constexpr int kAcanOff = kRS * kStage;                  // [2][kKC] canonical A tiles
+  static constexpr int kDwOff = kAcanOff + 2 * kKC * kM * 32;    // [2][kKC][128] dW, -1.5*2^23*dW
+  static constexpr int kMiscOff = kDwOff + 2 * 2 * kKC * kM * 4;
   static constexpr int kBytes = kMiscOff + 64;
+  static constexpr uint32_t kCols = 2 * kKC * NT;                // two TMEM groups of kKC blocks
 };
 
 __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
@@ -149,8 +150,23 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// One 18- or 34-byte block at a 2-byte aligned address: binary16 scale bits and
-// the 16 / 32 quant bytes as little-endian words, reading exactly its bytes.
+template <int NC>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[NC]);
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                 "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&v)[16]) {
+  tmem_ld16(taddr, v);
+}
+
+// One 18- or 34-byte block at a 2-byte aligned shared address: binary16 scale
+// bits and the 16 / 32 quant bytes as little-endian words, reading only its bytes.
 template <int BPB>
 __device__ __forceinline__ void read_block(const uint8_t* p, uint32_t& scale_bits, uint32_t (&q)[8]) {
   constexpr int nfull = BPB == 18 ? 4 : 8;
@@ -172,26 +188,31 @@ __device__ __forceinline__ void read_block(const uint8_t* p, uint32_t& scale_bit
 }
 
 template <int BPB, int NT>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kWarps * 32)
 qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilogue ep,
                 unsigned int* status) {
   using L = TcLayout<BPB, NT>;
+  constexpr int kHalf = NT / 2;  // columns drained per warp
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + L::kMiscOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff + 16);
+  float* dWs = reinterpret_cast<float*>(smem + L::kDwOff);  // [2][kKC][2][128]
 
-  constexpr uint32_t kCols = NT * 2 < 32 ? 32 : NT * 2;
   constexpr uint32_t kIdesc = (2u << 4) | ((BPB == 18 ? 0u : 1u) << 7) | (1u << 10) |
                               ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
 
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int quarter = warp & 3, colhalf = warp >> 2;
+  const int erow = blockIdx.y * kM + quarter * 32 + (tid & 31);  // epilogue row of this thread
+  const int urow = tid & (kM - 1);                               // unpack row of this thread
+  const int ublk = (tid >> 7) * 2;                               // first of its two blocks
   const int seq0 = blockIdx.x * NT;
-  const int row = blockIdx.y * kM + tid;
   const int nseq = min(NT, b.rows - seq0);
   const size_t row_bytes = (size_t)nb * BPB;
   const int nchunks = nb / kKC;
+  const uint8_t* wrow = w + (size_t)(blockIdx.y * kM + urow) * row_bytes;
 
-  if (warp == 0) tmem_alloc(tmem_slot, kCols);
+  if (warp == 0) tmem_alloc(tmem_slot, L::kCols);
   if (tid == 0) {
     mbar_init(&mbar[0], 1);
     mbar_init(&mbar[1], 1);
@@ -202,60 +223,57 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
   tc_after_sync();
   const uint32_t tmem_base = *tmem_slot;
 
-  // Stream chunk c (blocks 4c..4c+3) into ring stage c % kRS; always commits a
-  // group so that cp.async.wait_group counts stay uniform.
+  // Chunk c = blocks 4c..4c+3 into ring stage c % kRS; always one commit group.
   auto issue_chunk = [&](int c) {
     if (c < nchunks) {
       uint8_t* st = smem + (c % kRS) * L::kStage;
       const int blk0 = c * kKC;
-      const uint8_t* src = w + (size_t)row * row_bytes + (size_t)blk0 * BPB;
-      uint8_t* dst = st + tid * L::kRowRaw;
+      if (tid < kM) {
+        const uint8_t* src = wrow + (size_t)blk0 * BPB;
+        uint8_t* dst = st + tid * L::kRowRaw;
 #pragma unroll
-      for (int g = 0; g < kKC * BPB / 8; ++g) cp_async8(dst + 8 * g, src + 8 * g);
-      if (tid < NT) {
-        const bool valid = tid < nseq;
-        const size_t srow = valid ? (size_t)(seq0 + tid) : 0;
+        for (int g = 0; g < kKC * BPB / 8; ++g) cp_async8(dst + 8 * g, src + 8 * g);
+      } else if (tid - kM < NT) {
+        const int s = tid - kM;
+        const bool valid = s < nseq;
+        const size_t srow = valid ? (size_t)(seq0 + s) : 0;
         const int8_t* a = b.aq + srow * kActStride + (size_t)blk0 * 32;
 #pragma unroll
         for (int j = 0; j < kKC; ++j) {
-          cp_async16(st + L::kARaw + j * L::kBTile + tile_off(tid, 0), a + j * 32, valid);
-          cp_async16(st + L::kARaw + j * L::kBTile + tile_off(tid, 1), a + j * 32 + 16, valid);
+          cp_async16(st + L::kARaw + j * L::kBTile + tile_off(s, 0), a + j * 32, valid);
+          cp_async16(st + L::kARaw + j * L::kBTile + tile_off(s, 1), a + j * 32 + 16, valid);
         }
-        cp_async16(st + L::kDaOff + tid * kKC * 4, b.ad + srow * kActBlocks + blk0, valid);
-        cp_async16(st + L::kCOff + tid * kKC * 4, b.asum + srow * kActBlocks + blk0, valid);
+        cp_async16(st + L::kDaOff + s * kKC * 4, b.ad + srow * kActBlocks + blk0, valid);
+        cp_async16(st + L::kCOff + s * kKC * 4, b.asum + srow * kActBlocks + blk0, valid);
       }
     }
     cp_async_commit();
   };
-  auto issue_mma = [&](int blk) {
-    const uint8_t* A = smem + L::kAcanOff + (blk % kAbuf) * (kM * 32);
-    const uint8_t* B = smem + ((blk / kKC) % kRS) * L::kStage + L::kARaw + (blk % kKC) * L::kBTile;
-    mma_i8(tmem_base + (uint32_t)((blk & 1) * NT), smem_desc(A), smem_desc(B), kIdesc);
-    mma_commit(&mbar[blk & 1]);
-  };
 
-  float acc[NT];
+  float acc[kHalf];
 #pragma unroll
-  for (int s = 0; s < NT; ++s) acc[s] = 0.0f;
-  float dW_prev = 0.0f, negMdW_prev = 0.0f;
+  for (int s = 0; s < kHalf; ++s) acc[s] = 0.0f;
   uint32_t phase[2] = {0, 0};
-  int pending[2] = {0, 0};  // thread 0: committed MMAs not yet waited for
+  int pending[2] = {0, 0};  // thread 0: committed MMA groups not yet waited for
 
-  // Drains block `blk` (MMA already waited for) from TMEM into the accumulators.
-  auto epilogue = [&](int blk, float dW, float negMdW) {
-    const uint8_t* st = smem + ((blk / kKC) % kRS) * L::kStage;
+  // Drains chunk c's kKC blocks, in block order, into the accumulators.
+  auto epilogue = [&](int c) {
+    const uint8_t* st = smem + (c % kRS) * L::kStage;
     const float* dA = reinterpret_cast<const float*>(st + L::kDaOff);
     const int* C = reinterpret_cast<const int*>(st + L::kCOff);
-    const int j = blk % kKC;
-    const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)((blk & 1) * NT);
+    const float* dw = dWs + (c & 1) * (kKC * 2 * kM);
 #pragma unroll
-    for (int c0 = 0; c0 < NT; c0 += 16) {
-      uint32_t v[16];
-      tmem_ld16(taddr + c0, v);
+    for (int j = 0; j < kKC; ++j) {
+      const float dW = dw[(j * 2) * kM + quarter * 32 + (tid & 31)];
+      const float negMdW = dw[(j * 2 + 1) * kM + quarter * 32 + (tid & 31)];
+      uint32_t v[kHalf];
+      tmem_ld<kHalf>(tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                         (uint32_t)(((c & 1) * kKC + j) * NT + colhalf * kHalf),
+                     v);
       tmem_wait_ld();
 #pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        const int s = c0 + jj;
+      for (int jj = 0; jj < kHalf; ++jj) {
+        const int s = colhalf * kHalf + jj;
         const float da = dA[s * kKC + j];
         float t;
         if (BPB == 18) {
@@ -265,72 +283,82 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
           const float f = __fsub_rn(__int_as_float((int)v[jj] + 0x4B400000), 12582912.0f);
           t = __fmul_rn(f, __fmul_rn(dW, da));
         }
-        acc[s] = __fadd_rn(acc[s], t);
+        acc[jj] = __fadd_rn(acc[jj], t);
       }
     }
   };
 
   for (int c = 0; c < kRS; ++c) issue_chunk(c);
   int timed_out = 0;
-  int blk = 0;
-  for (; blk < nb; ++blk) {
-    const int c = blk / kKC, j = blk % kKC;
+  int c = 0;
+  for (; c < nchunks; ++c) {
     uint8_t* st = smem + (c % kRS) * L::kStage;
-    if (j == 0) {
-      cp_async_wait<kRS - 2>();
-      __syncthreads();
-      if (BPB == 18 && tid < NT) {
-        int* C = reinterpret_cast<int*>(st + L::kCOff);
+    // Chunk c has landed: groups issued so far end at chunk max(kRS-1, c+1).
+    cp_async_wait<kRS - 3>();
+    __syncthreads();
+    if (BPB == 18 && tid >= kM && tid - kM < NT) {
+      int* C = reinterpret_cast<int*>(st + L::kCOff) + (tid - kM) * kKC;
 #pragma unroll
-        for (int k = 0; k < kKC; ++k) C[tid * kKC + k] = 0x4B400000 - 8 * C[tid * kKC + k];
-      }
+      for (int k = 0; k < kKC; ++k) C[k] = 0x4B400000 - 8 * C[k];
     }
-    // unpack this thread's row of block blk into canonical A tile blk % kAbuf
-    uint32_t sb, q[8];
-    read_block<BPB>(st + tid * L::kRowRaw + j * BPB, sb, q);
-    const float dW = half_to_f32((uint16_t)sb);
-    const float negMdW = -__fmul_rn(12582912.0f, dW);
-    uint8_t* A = smem + L::kAcanOff + (blk % kAbuf) * (kM * 32);
-    if (BPB == 18) {
-      *reinterpret_cast<uint4*>(A + tile_off(tid, 0)) =
-          make_uint4(q[0] & 0x0f0f0f0fu, q[1] & 0x0f0f0f0fu, q[2] & 0x0f0f0f0fu, q[3] & 0x0f0f0f0fu);
-      *reinterpret_cast<uint4*>(A + tile_off(tid, 1)) =
-          make_uint4((q[0] >> 4) & 0x0f0f0f0fu, (q[1] >> 4) & 0x0f0f0f0fu,
-                     (q[2] >> 4) & 0x0f0f0f0fu, (q[3] >> 4) & 0x0f0f0f0fu);
-    } else {
-      *reinterpret_cast<uint4*>(A + tile_off(tid, 0)) = make_uint4(q[0], q[1], q[2], q[3]);
-      *reinterpret_cast<uint4*>(A + tile_off(tid, 1)) = make_uint4(q[4], q[5], q[6], q[7]);
+    // unpack two blocks of one row into the canonical A tiles of group c & 1
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int j = ublk + k;
+      uint32_t sb, q[8];
+      read_block<BPB>(st + urow * L::kRowRaw + j * BPB, sb, q);
+      const float dW = half_to_f32((uint16_t)sb);
+      float* dw = dWs + (c & 1) * (kKC * 2 * kM);
+      dw[(j * 2) * kM + urow] = dW;
+      dw[(j * 2 + 1) * kM + urow] = -__fmul_rn(12582912.0f, dW);
+      uint8_t* A = smem + L::kAcanOff + ((c & 1) * kKC + j) * (kM * 32);
+      if (BPB == 18) {
+        *reinterpret_cast<uint4*>(A + tile_off(urow, 0)) =
+            make_uint4(q[0] & 0x0f0f0f0fu, q[1] & 0x0f0f0f0fu, q[2] & 0x0f0f0f0fu, q[3] & 0x0f0f0f0fu);
+        *reinterpret_cast<uint4*>(A + tile_off(urow, 1)) =
+            make_uint4((q[0] >> 4) & 0x0f0f0f0fu, (q[1] >> 4) & 0x0f0f0f0fu,
+                       (q[2] >> 4) & 0x0f0f0f0fu, (q[3] >> 4) & 0x0f0f0f0fu);
+      } else {
+        *reinterpret_cast<uint4*>(A + tile_off(urow, 0)) = make_uint4(q[0], q[1], q[2], q[3]);
+        *reinterpret_cast<uint4*>(A + tile_off(urow, 1)) = make_uint4(q[4], q[5], q[6], q[7]);
+      }
     }
     fence_async_shared();
     tc_before_sync();
     const int stop = __syncthreads_or(timed_out);
     tc_after_sync();
     if (stop) break;
-    // every thread has drained block blk-2 (the last block of chunk c-1 when
-    // j == 1), so that chunk's ring stage can be refilled
-    if (j == 1 && c >= 1) issue_chunk(c - 1 + kRS);
-    if (tid == 0) { issue_mma(blk); pending[blk & 1] = 1; }
-    if (blk >= 1) {
-      const int pb = blk - 1;
-      if (!mbar_wait_bounded(&mbar[pb & 1], phase[pb & 1])) {
+    // Chunk c-2 was drained in iteration c-1 by every thread: refill its stage.
+    if (c >= 2) issue_chunk(c - 2 + kRS);
+    if (tid == 0) {
+#pragma unroll
+      for (int j = 0; j < kKC; ++j) {
+        const uint8_t* A = smem + L::kAcanOff + ((c & 1) * kKC + j) * (kM * 32);
+        const uint8_t* B = st + L::kARaw + j * L::kBTile;
+        mma_i8(tmem_base + (uint32_t)(((c & 1) * kKC + j) * NT), smem_desc(A), smem_desc(B), kIdesc);
+      }
+      mma_commit(&mbar[c & 1]);
+      pending[c & 1] = 1;
+    }
+    if (c >= 1) {
+      const int pc = c - 1;
+      if (!mbar_wait_bounded(&mbar[pc & 1], phase[pc & 1])) {
         timed_out = 1;
       } else {
-        phase[pb & 1] ^= 1u;
-        if (tid == 0) pending[pb & 1] = 0;
-        epilogue(pb, dW_prev, negMdW_prev);
+        phase[pc & 1] ^= 1u;
+        if (tid == 0) pending[pc & 1] = 0;
+        epilogue(pc);
       }
     }
-    dW_prev = dW;
-    negMdW_prev = negMdW;
   }
-  if (!timed_out && blk == nb) {
-    const int pb = nb - 1;
-    if (!mbar_wait_bounded(&mbar[pb & 1], phase[pb & 1])) {
+  if (!timed_out && c == nchunks) {
+    const int pc = nchunks - 1;
+    if (!mbar_wait_bounded(&mbar[pc & 1], phase[pc & 1])) {
       timed_out = 1;
     } else {
-      phase[pb & 1] ^= 1u;
-      if (tid == 0) pending[pb & 1] = 0;
-      epilogue(pb, dW_prev, negMdW_prev);
+      phase[pc & 1] ^= 1u;
+      if (tid == 0) pending[pc & 1] = 0;
+      epilogue(pc);
     }
   }
   cp_async_wait_all();
@@ -345,20 +373,21 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
   tc_before_sync();
   __syncthreads();
   tc_after_sync();
-  if (warp == 0) tmem_dealloc(tmem_base, kCols);
+  if (warp == 0) tmem_dealloc(tmem_base, L::kCols);
   if (aborted) return;
 
 #pragma unroll
-  for (int s = 0; s < NT; ++s) {
+  for (int jj = 0; jj < kHalf; ++jj) {
+    const int s = colhalf * kHalf + jj;
     if (s < nseq) {
       const int seq = seq0 + s;
-      float* dst = ep.out + (size_t)seq * ep.ld + row;
+      float* dst = ep.out + (size_t)seq * ep.ld + erow;
       float v;
-      if (ep.mode == EPI_BIAS) v = __fadd_rn(acc[s], ep.bias[row]);
-      else if (ep.mode == EPI_RESIDUAL) v = __fadd_rn(*dst, acc[s]);
-      else v = acc[s];
+      if (ep.mode == EPI_BIAS) v = __fadd_rn(acc[jj], ep.bias[erow]);
+      else if (ep.mode == EPI_RESIDUAL) v = __fadd_rn(*dst, acc[jj]);
+      else v = acc[jj];
       *dst = v;
-      check_finite(v, &ep.err[seq], ep.layer_ordinal, ep.domain, 0, row);
+      check_finite(v, &ep.err[seq], ep.layer_ordinal, ep.domain, 0, erow);
     }
   }
 }
@@ -366,14 +395,15 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
 template <int BPB, int NT>
 void launch_tc(const uint8_t* w, int rows, int nb, const Batch& b, const Epilogue& ep,
                unsigned int* status, cudaStream_t s) {
-  static bool configured = false;  // per process; the attribute is per function
+  static bool configured = false;  // one device per process
   if (!configured) {
     cudaFuncSetAttribute(qgemm_tc_kernel<BPB, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          TcLayout<BPB, NT>::kBytes);
     configured = true;
   }
   dim3 grid((b.rows + NT - 1) / NT, rows / kM);
-  qgemm_tc_kernel<BPB, NT><<<grid, kThreads, TcLayout<BPB, NT>::kBytes, s>>>(w, rows, nb, b, ep, status);
+  qgemm_tc_kernel<BPB, NT><<<grid, kWarps * 32, TcLayout<BPB, NT>::kBytes, s>>>(w, rows, nb, b, ep,
+                                                                                status);
 }
 
 }  // namespace
@@ -389,14 +419,12 @@ void launch_qgemm_tc(int wtype, const uint8_t* w, int rows, int columns, const B
   const int nb = columns / 32;
   const int rtiles = rows / kM;
   auto ctas = [&](int nt) { return rtiles * ((b.rows + nt - 1) / nt); };
-  const int nt = ctas(64) >= 296 ? 64 : ctas(32) >= 148 ? 32 : 16;
+  const int nt = ctas(32) >= 148 ? 32 : 16;
   if (wtype == W_Q4_0) {
-    if (nt == 64) launch_tc<18, 64>(w, rows, nb, b, ep, status, s);
-    else if (nt == 32) launch_tc<18, 32>(w, rows, nb, b, ep, status, s);
+    if (nt == 32) launch_tc<18, 32>(w, rows, nb, b, ep, status, s);
     else launch_tc<18, 16>(w, rows, nb, b, ep, status, s);
   } else {
-    if (nt == 64) launch_tc<34, 64>(w, rows, nb, b, ep, status, s);
-    else if (nt == 32) launch_tc<34, 32>(w, rows, nb, b, ep, status, s);
+    if (nt == 32) launch_tc<34, 32>(w, rows, nb, b, ep, status, s);
     else launch_tc<34, 16>(w, rows, nb, b, ep, status, s);
   }
 }

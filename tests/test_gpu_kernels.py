@@ -222,7 +222,7 @@ def test_matvec_shapes_match_oracle(wtype, rows, cols, batch):
 
 
 def test_tensor_core_widest_tile_matches_oracle():
-    """4864 x 896 Q4_0 at 512 rows selects the 64-sequence tile."""
+    """4864 x 896 Q4_0 at 512 rows: 16 sequence tiles per weight tile."""
     lib = _lib.load()
     rng = np.random.default_rng(512)
     rows, cols, batch = 4864, 896, 512
