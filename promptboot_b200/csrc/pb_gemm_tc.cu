@@ -116,7 +116,8 @@ constexpr int kM = 128;
 
 constexpr int kKC = 4;     // Q-blocks per cp.async chunk = MMAs per commit group
 constexpr int kRS = 4;     // chunk ring stages
-constexpr int kWarps = 8;  // two warps per TMEM lane quarter, each draining half the columns
+constexpr int kWarps = 16;     // four warps per TMEM lane quarter ...
+constexpr int kColGroups = 4;  // ... each draining a quarter of the columns
 
 template <int BPB, int NT>
 struct TcLayout {
@@ -152,6 +153,13 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 
 template <int NC>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[NC]);
+template <>
+__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&v)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(taddr)
+               : "memory");
+}
 template <>
 __device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&v)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -192,7 +200,7 @@ __global__ void __launch_bounds__(kWarps * 32)
 qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilogue ep,
                 unsigned int* status) {
   using L = TcLayout<BPB, NT>;
-  constexpr int kHalf = NT / 2;  // columns drained per warp
+  constexpr int kHalf = NT / kColGroups;  // columns drained per warp
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + L::kMiscOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff + 16);
@@ -205,7 +213,7 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
   const int quarter = warp & 3, colhalf = warp >> 2;
   const int erow = blockIdx.y * kM + quarter * 32 + (tid & 31);  // epilogue row of this thread
   const int urow = tid & (kM - 1);                               // unpack row of this thread
-  const int ublk = (tid >> 7) * 2;                               // first of its two blocks
+  const int ublk = tid >> 7;                                     // its block within the chunk
   const int seq0 = blockIdx.x * NT;
   const int nseq = min(NT, b.rows - seq0);
   const size_t row_bytes = (size_t)nb * BPB;
@@ -259,31 +267,44 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
   // Drains chunk c's kKC blocks, in block order, into the accumulators.
   auto epilogue = [&](int c) {
     const uint8_t* st = smem + (c % kRS) * L::kStage;
-    const float* dA = reinterpret_cast<const float*>(st + L::kDaOff);
-    const int* C = reinterpret_cast<const int*>(st + L::kCOff);
+    const float4* dA4 = reinterpret_cast<const float4*>(st + L::kDaOff);
+    const int4* C4 = reinterpret_cast<const int4*>(st + L::kCOff);
     const float* dw = dWs + (c & 1) * (kKC * 2 * kM);
+    const int lrow = quarter * 32 + (tid & 31);
+    uint32_t v[kKC][kHalf];
 #pragma unroll
-    for (int j = 0; j < kKC; ++j) {
-      const float dW = dw[(j * 2) * kM + quarter * 32 + (tid & 31)];
-      const float negMdW = dw[(j * 2 + 1) * kM + quarter * 32 + (tid & 31)];
-      uint32_t v[kHalf];
+    for (int j = 0; j < kKC; ++j)
       tmem_ld<kHalf>(tmem_base + ((uint32_t)(quarter * 32) << 16) +
                          (uint32_t)(((c & 1) * kKC + j) * NT + colhalf * kHalf),
-                     v);
-      tmem_wait_ld();
+                     v[j]);
+    tmem_wait_ld();
+    float dW[kKC], negMdW[kKC];
 #pragma unroll
-      for (int jj = 0; jj < kHalf; ++jj) {
-        const int s = colhalf * kHalf + jj;
-        const float da = dA[s * kKC + j];
+    for (int j = 0; j < kKC; ++j) {
+      dW[j] = dw[(j * 2) * kM + lrow];
+      negMdW[j] = dw[(j * 2 + 1) * kM + lrow];
+    }
+#pragma unroll
+    for (int jj = 0; jj < kHalf; ++jj) {
+      const int s = colhalf * kHalf + jj;
+      const float4 da4 = dA4[s];  // the column's scales for the chunk's 4 blocks
+      const float da[4] = {da4.x, da4.y, da4.z, da4.w};
+      int cc[4] = {0, 0, 0, 0};
+      if (BPB == 18) {
+        const int4 c4 = C4[s];
+        cc[0] = c4.x; cc[1] = c4.y; cc[2] = c4.z; cc[3] = c4.w;
+      }
+#pragma unroll
+      for (int j = 0; j < kKC; ++j) {
         float t;
         if (BPB == 18) {
-          const float x = __int_as_float((int)v[jj] + C[s * kKC + j]);
-          t = __fmul_rn(__fmaf_rn(x, dW, negMdW), da);
+          const float x = __int_as_float((int)v[j][jj] + cc[j]);
+          t = __fmul_rn(__fmaf_rn(x, dW[j], negMdW[j]), da[j]);
         } else {
-          const float f = __fsub_rn(__int_as_float((int)v[jj] + 0x4B400000), 12582912.0f);
-          t = __fmul_rn(f, __fmul_rn(dW, da));
+          const float f = __fsub_rn(__int_as_float((int)v[j][jj] + 0x4B400000), 12582912.0f);
+          t = __fmul_rn(f, __fmul_rn(dW[j], da[j]));
         }
-        acc[jj] = __fadd_rn(acc[jj], t);
+        acc[jj] = __fadd_rn(acc[jj], t);  // blocks in order per column
       }
     }
   };
@@ -301,10 +322,9 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
 #pragma unroll
       for (int k = 0; k < kKC; ++k) C[k] = 0x4B400000 - 8 * C[k];
     }
-    // unpack two blocks of one row into the canonical A tiles of group c & 1
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int j = ublk + k;
+    // unpack one block of one row into the canonical A tiles of group c & 1
+    {
+      const int j = ublk;
       uint32_t sb, q[8];
       read_block<BPB>(st + urow * L::kRowRaw + j * BPB, sb, q);
       const float dW = half_to_f32((uint16_t)sb);
