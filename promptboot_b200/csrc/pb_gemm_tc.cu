@@ -17,12 +17,14 @@
 // Shared-memory tiles use the canonical no-swizzle K-major layout: 8-row x
 // 16-byte core matrices, the two 16-byte K halves of an 8-row group adjacent
 // (leading byte offset 128), groups 256 bytes apart (stride byte offset 256).
-// Operands stream in through a 4-stage cp.async ring of 4-block chunks: raw
-// weight bytes (8-byte granules; 18- and 34-byte blocks are only 2-byte
-// aligned) are unpacked by the threads into the canonical A tile, while the
-// activation rows are scattered by 16-byte cp.async straight into the canonical
-// B layout.  Every mbarrier wait is bounded; a timeout sets *status, stops
-// issuing, waits (bounded) for work in flight, frees TMEM and returns.
+// Warp-specialised pipeline over 4-block chunks, chained by mbarriers only: a
+// loader warp streams raw weight bytes (8-byte cp.async granules; 18- and
+// 34-byte blocks are only 2-byte aligned) and scatters activation rows by 16-byte
+// cp.async straight into the canonical B layout, four unpack warps turn the raw
+// weights into the canonical A tile, one thread issues the four MMAs of a chunk
+// with one commit, and eight epilogue warps drain the TMEM group.  Every wait is
+// bounded (200 ms on %globaltimer, or another role's abort); an abort sets
+// *status, lets committed MMAs finish (bounded), frees TMEM and returns.
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
 
@@ -45,12 +47,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
-}
-// Bounded wait: false after ~2^22 polls (seconds); the caller aborts.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < (1u << 22); ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
 }
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -114,10 +110,13 @@ __device__ __forceinline__ int tile_off(int row, int half) {
 
 constexpr int kM = 128;
 
-constexpr int kKC = 4;     // Q-blocks per cp.async chunk = MMAs per commit group
-constexpr int kRS = 4;     // chunk ring stages
-constexpr int kWarps = 16;     // four warps per TMEM lane quarter ...
-constexpr int kColGroups = 4;  // ... each draining a quarter of the columns
+constexpr int kKC = 4;  // Q-blocks per chunk = MMAs per commit
+constexpr int kRS = 4;  // ring stages
+// Warp roles: one cp.async loader, one MMA issuer, four unpackers (one weight
+// row each), eight epilogue warps (two per TMEM lane quarter, half the columns each).
+constexpr int kLoaderWarp = 0, kMmaWarp = 1, kUnpackWarp0 = 2, kEpiWarp0 = 6;
+constexpr int kUnpackWarps = 4, kEpiWarps = 8;
+constexpr int kWsThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 448
 
 template <int BPB, int NT>
 struct TcLayout {
@@ -127,13 +126,13 @@ struct TcLayout {
   static constexpr int kBRaw = kKC * kBTile;
   static constexpr int kScale = NT * kKC * 4;
   static constexpr int kDaOff = kARaw + kBRaw;
-  static constexpr int kCOff = kDaOff + kScale;
-  static constexpr int kStage = kCOff + kScale;
-  static constexpr int kAcanOff = kRS * kStage;                  // [2][kKC] canonical A tiles
-  static constexpr int kDwOff = kAcanOff + 2 * kKC * kM * 32;    // [2][kKC][128] dW, -1.5*2^23*dW
-  static constexpr int kMiscOff = kDwOff + 2 * 2 * kKC * kM * 4;
-  static constexpr int kBytes = kMiscOff + 64;
-  static constexpr uint32_t kCols = 2 * kKC * NT;                // two TMEM groups of kKC blocks
+  static constexpr int kSumOff = kDaOff + kScale;
+  static constexpr int kStage = kSumOff + kScale;
+  static constexpr int kAcanOff = kRS * kStage;               // [2][kKC] canonical A tiles
+  static constexpr int kBarOff = kAcanOff + 2 * kKC * kM * 32;
+  static constexpr int kSlotOff = kBarOff + (2 * kRS + 8) * 8;
+  static constexpr int kBytes = kSlotOff + 16;
+  static constexpr uint32_t kCols = 2 * kKC * NT;             // two TMEM groups of kKC blocks
 };
 
 __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
@@ -144,22 +143,42 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
                "r"(valid ? 16 : 0)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// Arrives on `bar` once every cp.async this thread issued so far has landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Waits for the phase of `bar` with the given parity.  Gives up when another
+// role has aborted, or after 200 ms (then aborts every role); false = give up.
+__device__ __noinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t deadline = global_ns() + 200000000ull;
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() > deadline) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// wait_phase for a whole warp: every lane gets the same answer, so the warp
+// never splits around the .sync.aligned instructions that follow.
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, wait_phase(bar, parity, abort_flag));
+}
 
 template <int NC>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[NC]);
-template <>
-__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&v)[4]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-               : "r"(taddr)
-               : "memory");
-}
 template <>
 __device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&v)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -172,11 +191,18 @@ template <>
 __device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&v)[16]) {
   tmem_ld16(taddr, v);
 }
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&v)[32]) {
+  uint32_t (&lo)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[0]);
+  uint32_t (&hi)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[16]);
+  tmem_ld16(taddr, lo);
+  tmem_ld16(taddr + 16, hi);
+}
 
-// One 18- or 34-byte block at a 2-byte aligned shared address: binary16 scale
-// bits and the 16 / 32 quant bytes as little-endian words, reading only its bytes.
+// One 18- or 34-byte block at a 2-byte aligned shared address: the 16 / 32
+// quant bytes as little-endian words, reading only the block's bytes.
 template <int BPB>
-__device__ __forceinline__ void read_block(const uint8_t* p, uint32_t& scale_bits, uint32_t (&q)[8]) {
+__device__ __forceinline__ void read_quants(const uint8_t* p, uint32_t (&q)[8]) {
   constexpr int nfull = BPB == 18 ? 4 : 8;
   if ((smem_u32(p) & 3) == 0) {
     const uint32_t* p4 = reinterpret_cast<const uint32_t*>(p);
@@ -184,11 +210,9 @@ __device__ __forceinline__ void read_block(const uint8_t* p, uint32_t& scale_bit
 #pragma unroll
     for (int i = 0; i < nfull; ++i) words[i] = p4[i];
     words[nfull] = *reinterpret_cast<const uint16_t*>(p + 4 * nfull);
-    scale_bits = words[0] & 0xffffu;
 #pragma unroll
     for (int i = 0; i < nfull; ++i) q[i] = __funnelshift_r(words[i], words[i + 1], 16);
   } else {
-    scale_bits = *reinterpret_cast<const uint16_t*>(p);
     const uint32_t* p4 = reinterpret_cast<const uint32_t*>(p + 2);
 #pragma unroll
     for (int i = 0; i < nfull; ++i) q[i] = p4[i];
@@ -196,34 +220,44 @@ __device__ __forceinline__ void read_block(const uint8_t* p, uint32_t& scale_bit
 }
 
 template <int BPB, int NT>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWsThreads, NT <= 16 ? 2 : 1)
 qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilogue ep,
                 unsigned int* status) {
   using L = TcLayout<BPB, NT>;
-  constexpr int kHalf = NT / kColGroups;  // columns drained per warp
+  constexpr int kHalf = NT / 2;
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + L::kMiscOff);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff + 16);
-  float* dWs = reinterpret_cast<float*>(smem + L::kDwOff);  // [2][kKC][2][128]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);  // raw chunk landed
+  uint64_t* empty = full + kRS;                                        // ring stage free
+  uint64_t* afull = empty + kRS;                                       // canonical A ready [2]
+  uint64_t* aempty = afull + 2;                                        // canonical A free [2]
+  uint64_t* tfull = aempty + 2;                                        // TMEM group ready [2]
+  uint64_t* tempty = tfull + 2;                                        // TMEM group drained [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kSlotOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kSlotOff + 4);
 
   constexpr uint32_t kIdesc = (2u << 4) | ((BPB == 18 ? 0u : 1u) << 7) | (1u << 10) |
                               ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int quarter = warp & 3, colhalf = warp >> 2;
-  const int erow = blockIdx.y * kM + quarter * 32 + (tid & 31);  // epilogue row of this thread
-  const int urow = tid & (kM - 1);                               // unpack row of this thread
-  const int ublk = tid >> 7;                                     // its block within the chunk
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int seq0 = blockIdx.x * NT;
+  const int row0 = blockIdx.y * kM;
   const int nseq = min(NT, b.rows - seq0);
   const size_t row_bytes = (size_t)nb * BPB;
   const int nchunks = nb / kKC;
-  const uint8_t* wrow = w + (size_t)(blockIdx.y * kM + urow) * row_bytes;
 
-  if (warp == 0) tmem_alloc(tmem_slot, L::kCols);
-  if (tid == 0) {
-    mbar_init(&mbar[0], 1);
-    mbar_init(&mbar[1], 1);
+  if (warp == kLoaderWarp) tmem_alloc(tmem_slot, L::kCols);
+  if (tid == kMmaWarp * 32) {
+    for (int st = 0; st < kRS; ++st) {
+      mbar_init(&full[st], 32);
+      mbar_init(&empty[st], kUnpackWarps + kEpiWarps);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&afull[g], kUnpackWarps);
+      mbar_init(&aempty[g], 1);
+      mbar_init(&tfull[g], 1);
+      mbar_init(&tempty[g], kEpiWarps);
+    }
+    *abort_flag = 0;
     fence_barrier_init();
   }
   tc_before_sync();
@@ -231,183 +265,182 @@ qgemm_tc_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilog
   tc_after_sync();
   const uint32_t tmem_base = *tmem_slot;
 
-  // Chunk c = blocks 4c..4c+3 into ring stage c % kRS; always one commit group.
-  auto issue_chunk = [&](int c) {
-    if (c < nchunks) {
-      uint8_t* st = smem + (c % kRS) * L::kStage;
-      const int blk0 = c * kKC;
-      if (tid < kM) {
-        const uint8_t* src = wrow + (size_t)blk0 * BPB;
-        uint8_t* dst = st + tid * L::kRowRaw;
+  float acc[kHalf];
 #pragma unroll
-        for (int g = 0; g < kKC * BPB / 8; ++g) cp_async8(dst + 8 * g, src + 8 * g);
-      } else if (tid - kM < NT) {
-        const int s = tid - kM;
+  for (int s = 0; s < kHalf; ++s) acc[s] = 0.0f;
+  int mma_last = -1;  // MMA lane: last chunk committed
+
+  if (warp == kLoaderWarp) {
+    for (int c = 0; c < nchunks; ++c) {
+      const int st = c % kRS;
+      if (!wait_warp(&empty[st], ((c / kRS) & 1) ^ 1, abort_flag)) break;
+      uint8_t* sp = smem + st * L::kStage;
+      const int blk0 = c * kKC;
+#pragma unroll
+      for (int rr = 0; rr < kM / 32; ++rr) {
+        const int r = lane + 32 * rr;
+        const uint8_t* src = w + (size_t)(row0 + r) * row_bytes + (size_t)blk0 * BPB;
+        uint8_t* dst = sp + r * L::kRowRaw;
+#pragma unroll
+        for (int gch = 0; gch < kKC * BPB / 8; ++gch) cp_async8(dst + 8 * gch, src + 8 * gch);
+      }
+      for (int s = lane; s < NT; s += 32) {
         const bool valid = s < nseq;
         const size_t srow = valid ? (size_t)(seq0 + s) : 0;
         const int8_t* a = b.aq + srow * kActStride + (size_t)blk0 * 32;
 #pragma unroll
         for (int j = 0; j < kKC; ++j) {
-          cp_async16(st + L::kARaw + j * L::kBTile + tile_off(s, 0), a + j * 32, valid);
-          cp_async16(st + L::kARaw + j * L::kBTile + tile_off(s, 1), a + j * 32 + 16, valid);
+          cp_async16(sp + L::kARaw + j * L::kBTile + tile_off(s, 0), a + j * 32, valid);
+          cp_async16(sp + L::kARaw + j * L::kBTile + tile_off(s, 1), a + j * 32 + 16, valid);
         }
-        cp_async16(st + L::kDaOff + s * kKC * 4, b.ad + srow * kActBlocks + blk0, valid);
-        cp_async16(st + L::kCOff + s * kKC * 4, b.asum + srow * kActBlocks + blk0, valid);
+        cp_async16(sp + L::kDaOff + s * kKC * 4, b.ad + srow * kActBlocks + blk0, valid);
+        cp_async16(sp + L::kSumOff + s * kKC * 4, b.asum + srow * kActBlocks + blk0, valid);
+      }
+      cp_async_arrive(&full[st]);
+    }
+    cp_async_wait_all();
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      for (int c = 0; c < nchunks; ++c) {
+        const int g = c & 1, st = c % kRS, k2 = c >> 1;
+        if (!wait_phase(&afull[g], k2 & 1, abort_flag)) break;
+        if (!wait_phase(&tempty[g], (k2 & 1) ^ 1, abort_flag)) break;
+        if (!wait_phase(&full[st], (c / kRS) & 1, abort_flag)) break;
+        fence_async_shared();
+        tc_after_sync();
+        const uint8_t* bst = smem + st * L::kStage + L::kARaw;
+#pragma unroll
+        for (int j = 0; j < kKC; ++j) {
+          const uint8_t* A = smem + L::kAcanOff + (g * kKC + j) * (kM * 32);
+          mma_i8(tmem_base + (uint32_t)((g * kKC + j) * NT), smem_desc(A),
+                 smem_desc(bst + j * L::kBTile), kIdesc);
+        }
+        mma_commit(&aempty[g]);
+        mma_commit(&tfull[g]);
+        mma_last = c;
       }
     }
-    cp_async_commit();
-  };
-
-  float acc[kHalf];
-#pragma unroll
-  for (int s = 0; s < kHalf; ++s) acc[s] = 0.0f;
-  uint32_t phase[2] = {0, 0};
-  int pending[2] = {0, 0};  // thread 0: committed MMA groups not yet waited for
-
-  // Drains chunk c's kKC blocks, in block order, into the accumulators.
-  auto epilogue = [&](int c) {
-    const uint8_t* st = smem + (c % kRS) * L::kStage;
-    const float4* dA4 = reinterpret_cast<const float4*>(st + L::kDaOff);
-    const int4* C4 = reinterpret_cast<const int4*>(st + L::kCOff);
-    const float* dw = dWs + (c & 1) * (kKC * 2 * kM);
-    const int lrow = quarter * 32 + (tid & 31);
-    uint32_t v[kKC][kHalf];
-#pragma unroll
-    for (int j = 0; j < kKC; ++j)
-      tmem_ld<kHalf>(tmem_base + ((uint32_t)(quarter * 32) << 16) +
-                         (uint32_t)(((c & 1) * kKC + j) * NT + colhalf * kHalf),
-                     v[j]);
-    tmem_wait_ld();
-    float dW[kKC], negMdW[kKC];
-#pragma unroll
-    for (int j = 0; j < kKC; ++j) {
-      dW[j] = dw[(j * 2) * kM + lrow];
-      negMdW[j] = dw[(j * 2 + 1) * kM + lrow];
-    }
-#pragma unroll
-    for (int jj = 0; jj < kHalf; ++jj) {
-      const int s = colhalf * kHalf + jj;
-      const float4 da4 = dA4[s];  // the column's scales for the chunk's 4 blocks
-      const float da[4] = {da4.x, da4.y, da4.z, da4.w};
-      int cc[4] = {0, 0, 0, 0};
-      if (BPB == 18) {
-        const int4 c4 = C4[s];
-        cc[0] = c4.x; cc[1] = c4.y; cc[2] = c4.z; cc[3] = c4.w;
-      }
+    __syncwarp();
+  } else if (warp < kEpiWarp0) {
+    const int u = tid - kUnpackWarp0 * 32;  // weight row of this thread
+    for (int c = 0; c < nchunks; ++c) {
+      const int g = c & 1, st = c % kRS, k2 = c >> 1;
+      if (!wait_warp(&full[st], (c / kRS) & 1, abort_flag)) break;
+      if (!wait_warp(&aempty[g], (k2 & 1) ^ 1, abort_flag)) break;
+      const uint8_t* raw = smem + st * L::kStage + u * L::kRowRaw;
 #pragma unroll
       for (int j = 0; j < kKC; ++j) {
-        float t;
+        uint32_t q[8];
+        read_quants<BPB>(raw + j * BPB, q);
+        uint8_t* A = smem + L::kAcanOff + (g * kKC + j) * (kM * 32);
         if (BPB == 18) {
-          const float x = __int_as_float((int)v[j][jj] + cc[j]);
-          t = __fmul_rn(__fmaf_rn(x, dW[j], negMdW[j]), da[j]);
+          *reinterpret_cast<uint4*>(A + tile_off(u, 0)) =
+              make_uint4(q[0] & 0x0f0f0f0fu, q[1] & 0x0f0f0f0fu, q[2] & 0x0f0f0f0fu, q[3] & 0x0f0f0f0fu);
+          *reinterpret_cast<uint4*>(A + tile_off(u, 1)) =
+              make_uint4((q[0] >> 4) & 0x0f0f0f0fu, (q[1] >> 4) & 0x0f0f0f0fu,
+                         (q[2] >> 4) & 0x0f0f0f0fu, (q[3] >> 4) & 0x0f0f0f0fu);
         } else {
-          const float f = __fsub_rn(__int_as_float((int)v[j][jj] + 0x4B400000), 12582912.0f);
-          t = __fmul_rn(f, __fmul_rn(dW[j], da[j]));
+          *reinterpret_cast<uint4*>(A + tile_off(u, 0)) = make_uint4(q[0], q[1], q[2], q[3]);
+          *reinterpret_cast<uint4*>(A + tile_off(u, 1)) = make_uint4(q[4], q[5], q[6], q[7]);
         }
-        acc[jj] = __fadd_rn(acc[jj], t);  // blocks in order per column
+      }
+      fence_async_shared();  // generic-proxy tile writes -> tensor core
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&afull[g]);
+        mbar_arrive(&empty[st]);
       }
     }
-  };
-
-  for (int c = 0; c < kRS; ++c) issue_chunk(c);
-  int timed_out = 0;
-  int c = 0;
-  for (; c < nchunks; ++c) {
-    uint8_t* st = smem + (c % kRS) * L::kStage;
-    // Chunk c has landed: groups issued so far end at chunk max(kRS-1, c+1).
-    cp_async_wait<kRS - 3>();
-    __syncthreads();
-    if (BPB == 18 && tid >= kM && tid - kM < NT) {
-      int* C = reinterpret_cast<int*>(st + L::kCOff) + (tid - kM) * kKC;
-#pragma unroll
-      for (int k = 0; k < kKC; ++k) C[k] = 0x4B400000 - 8 * C[k];
-    }
-    // unpack one block of one row into the canonical A tiles of group c & 1
-    {
-      const int j = ublk;
-      uint32_t sb, q[8];
-      read_block<BPB>(st + urow * L::kRowRaw + j * BPB, sb, q);
-      const float dW = half_to_f32((uint16_t)sb);
-      float* dw = dWs + (c & 1) * (kKC * 2 * kM);
-      dw[(j * 2) * kM + urow] = dW;
-      dw[(j * 2 + 1) * kM + urow] = -__fmul_rn(12582912.0f, dW);
-      uint8_t* A = smem + L::kAcanOff + ((c & 1) * kKC + j) * (kM * 32);
-      if (BPB == 18) {
-        *reinterpret_cast<uint4*>(A + tile_off(urow, 0)) =
-            make_uint4(q[0] & 0x0f0f0f0fu, q[1] & 0x0f0f0f0fu, q[2] & 0x0f0f0f0fu, q[3] & 0x0f0f0f0fu);
-        *reinterpret_cast<uint4*>(A + tile_off(urow, 1)) =
-            make_uint4((q[0] >> 4) & 0x0f0f0f0fu, (q[1] >> 4) & 0x0f0f0f0fu,
-                       (q[2] >> 4) & 0x0f0f0f0fu, (q[3] >> 4) & 0x0f0f0f0fu);
-      } else {
-        *reinterpret_cast<uint4*>(A + tile_off(urow, 0)) = make_uint4(q[0], q[1], q[2], q[3]);
-        *reinterpret_cast<uint4*>(A + tile_off(urow, 1)) = make_uint4(q[4], q[5], q[6], q[7]);
-      }
-    }
-    fence_async_shared();
-    tc_before_sync();
-    const int stop = __syncthreads_or(timed_out);
-    tc_after_sync();
-    if (stop) break;
-    // Chunk c-2 was drained in iteration c-1 by every thread: refill its stage.
-    if (c >= 2) issue_chunk(c - 2 + kRS);
-    if (tid == 0) {
+  } else {
+    // Epilogue warp: TMEM lanes of its quarter (warp % 4 by the tcgen05.ld rule),
+    // half of the chunk's columns, 16 columns x 4 blocks per TMEM batch.
+    static_assert(kKC == 4, "float4 scale loads assume 4 blocks per chunk");
+    constexpr int kSub = kHalf < 16 ? kHalf : 16;
+    const int quarter = warp & 3, colhalf = (warp - kEpiWarp0) >> 2;
+    const int lrow = quarter * 32 + lane;
+    for (int c = 0; c < nchunks; ++c) {
+      const int g = c & 1, st = c % kRS, k2 = c >> 1;
+      if (!wait_warp(&tfull[g], k2 & 1, abort_flag)) break;
+      if (!wait_warp(&full[st], (c / kRS) & 1, abort_flag)) break;
+      tc_after_sync();
+      const uint8_t* sp = smem + st * L::kStage;
+      const float4* dA4 = reinterpret_cast<const float4*>(sp + L::kDaOff);
+      const int4* asum4 = reinterpret_cast<const int4*>(sp + L::kSumOff);
+      float dW[kKC], negMdW[kKC];
 #pragma unroll
       for (int j = 0; j < kKC; ++j) {
-        const uint8_t* A = smem + L::kAcanOff + ((c & 1) * kKC + j) * (kM * 32);
-        const uint8_t* B = st + L::kARaw + j * L::kBTile;
-        mma_i8(tmem_base + (uint32_t)(((c & 1) * kKC + j) * NT), smem_desc(A), smem_desc(B), kIdesc);
+        dW[j] = half_to_f32(*reinterpret_cast<const uint16_t*>(sp + lrow * L::kRowRaw + j * BPB));
+        negMdW[j] = -__fmul_rn(12582912.0f, dW[j]);
       }
-      mma_commit(&mbar[c & 1]);
-      pending[c & 1] = 1;
-    }
-    if (c >= 1) {
-      const int pc = c - 1;
-      if (!mbar_wait_bounded(&mbar[pc & 1], phase[pc & 1])) {
-        timed_out = 1;
-      } else {
-        phase[pc & 1] ^= 1u;
-        if (tid == 0) pending[pc & 1] = 0;
-        epilogue(pc);
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(g * kKC * NT);
+#pragma unroll
+      for (int sb = 0; sb < kHalf; sb += kSub) {
+        uint32_t v[kKC][kSub];
+#pragma unroll
+        for (int j = 0; j < kKC; ++j) tmem_ld<kSub>(tbase + (uint32_t)(j * NT + colhalf * kHalf + sb), v[j]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int jj = 0; jj < kSub; ++jj) {
+          const int s = colhalf * kHalf + sb + jj;
+          const float4 da = dA4[s];
+          const float dav[4] = {da.x, da.y, da.z, da.w};
+          float a = acc[sb + jj];
+          if (BPB == 18) {
+            const int4 sm = asum4[s];
+            const int smv[4] = {sm.x, sm.y, sm.z, sm.w};
+#pragma unroll
+            for (int j = 0; j < kKC; ++j) {
+              const float x = __int_as_float((int)v[j][jj] + 0x4B400000 - 8 * smv[j]);
+              a = __fadd_rn(a, __fmul_rn(__fmaf_rn(x, dW[j], negMdW[j]), dav[j]));
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < kKC; ++j) {
+              const float f = __fsub_rn(__int_as_float((int)v[j][jj] + 0x4B400000), 12582912.0f);
+              a = __fadd_rn(a, __fmul_rn(f, __fmul_rn(dW[j], dav[j])));
+            }
+          }
+          acc[sb + jj] = a;  // blocks in order per column
+        }
+      }
+      tc_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&tempty[g]);
+        mbar_arrive(&empty[st]);
       }
     }
   }
-  if (!timed_out && c == nchunks) {
-    const int pc = nchunks - 1;
-    if (!mbar_wait_bounded(&mbar[pc & 1], phase[pc & 1])) {
-      timed_out = 1;
-    } else {
-      phase[pc & 1] ^= 1u;
-      if (tid == 0) pending[pc & 1] = 0;
-      epilogue(pc);
+
+  __syncthreads();
+  const bool aborted = *abort_flag != 0;
+  if (aborted && warp == kMmaWarp && lane == 0 && mma_last >= 0) {
+    // MMAs already committed must finish before their TMEM is released.
+    const uint64_t deadline = global_ns() + 50000000ull;
+    while (!mbar_try_wait(&tfull[mma_last & 1], (mma_last >> 1) & 1) && global_ns() < deadline) {
     }
   }
-  cp_async_wait_all();
-  tc_before_sync();
-  const int aborted = __syncthreads_or(timed_out);
-  tc_after_sync();
-  if (aborted && tid == 0) {
-    atomicOr(status, 1u);
-    for (int k = 0; k < 2; ++k)
-      if (pending[k]) mbar_wait_bounded(&mbar[k], phase[k]);
-  }
+  if (aborted && tid == 0) atomicOr(status, 1u);
   tc_before_sync();
   __syncthreads();
   tc_after_sync();
-  if (warp == 0) tmem_dealloc(tmem_base, L::kCols);
-  if (aborted) return;
+  if (warp == kLoaderWarp) tmem_dealloc(tmem_base, L::kCols);
+  if (aborted || warp < kEpiWarp0) return;
 
+  const int row = row0 + (warp & 3) * 32 + lane;
+  const int colhalf = (warp - kEpiWarp0) >> 2;
 #pragma unroll
   for (int jj = 0; jj < kHalf; ++jj) {
     const int s = colhalf * kHalf + jj;
     if (s < nseq) {
       const int seq = seq0 + s;
-      float* dst = ep.out + (size_t)seq * ep.ld + erow;
+      float* dst = ep.out + (size_t)seq * ep.ld + row;
       float v;
-      if (ep.mode == EPI_BIAS) v = __fadd_rn(acc[jj], ep.bias[erow]);
+      if (ep.mode == EPI_BIAS) v = __fadd_rn(acc[jj], ep.bias[row]);
       else if (ep.mode == EPI_RESIDUAL) v = __fadd_rn(*dst, acc[jj]);
       else v = acc[jj];
       *dst = v;
-      check_finite(v, &ep.err[seq], ep.layer_ordinal, ep.domain, 0, erow);
+      check_finite(v, &ep.err[seq], ep.layer_ordinal, ep.domain, 0, row);
     }
   }
 }
@@ -422,8 +455,8 @@ void launch_tc(const uint8_t* w, int rows, int nb, const Batch& b, const Epilogu
     configured = true;
   }
   dim3 grid((b.rows + NT - 1) / NT, rows / kM);
-  qgemm_tc_kernel<BPB, NT><<<grid, kWarps * 32, TcLayout<BPB, NT>::kBytes, s>>>(w, rows, nb, b, ep,
-                                                                                status);
+  qgemm_tc_kernel<BPB, NT><<<grid, kWsThreads, TcLayout<BPB, NT>::kBytes, s>>>(w, rows, nb, b, ep,
+                                                                              status);
 }
 
 }  // namespace
@@ -439,12 +472,14 @@ void launch_qgemm_tc(int wtype, const uint8_t* w, int rows, int columns, const B
   const int nb = columns / 32;
   const int rtiles = rows / kM;
   auto ctas = [&](int nt) { return rtiles * ((b.rows + nt - 1) / nt); };
-  const int nt = ctas(32) >= 148 ? 32 : 16;
+  const int nt = ctas(64) >= 296 ? 64 : ctas(32) >= 148 ? 32 : 16;
   if (wtype == W_Q4_0) {
-    if (nt == 32) launch_tc<18, 32>(w, rows, nb, b, ep, status, s);
+    if (nt == 64) launch_tc<18, 64>(w, rows, nb, b, ep, status, s);
+    else if (nt == 32) launch_tc<18, 32>(w, rows, nb, b, ep, status, s);
     else launch_tc<18, 16>(w, rows, nb, b, ep, status, s);
   } else {
-    if (nt == 32) launch_tc<34, 32>(w, rows, nb, b, ep, status, s);
+    if (nt == 64) launch_tc<34, 64>(w, rows, nb, b, ep, status, s);
+    else if (nt == 32) launch_tc<34, 32>(w, rows, nb, b, ep, status, s);
     else launch_tc<34, 16>(w, rows, nb, b, ep, status, s);
   }
 }
