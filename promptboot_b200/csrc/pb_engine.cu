@@ -13,6 +13,7 @@
 #include "pb_kernels.cuh"
 
 #include <algorithm>
+#include <initializer_list>
 #include <vector>
 
 namespace {
@@ -133,6 +134,9 @@ struct pb_engine {
   int8_t* aq = nullptr;
   float* ad = nullptr;
   int* asum = nullptr;
+  int8_t* aq_tc = nullptr;  // tensor-core activation layout (pb_kernels.cuh Batch)
+  float* ad_tc = nullptr;
+  int tc_seqs = 0;
   int *d_slots = nullptr, *d_positions = nullptr;
   uint32_t* d_tokens = nullptr;
   unsigned long long* d_err = nullptr;      // [kErrSteps][max_seqs]
@@ -194,18 +198,6 @@ struct pb_engine {
                     151936 * 4) + (size_t)14 * (capacity + 4) * 4;
   }
 
-  pb::Batch batch(uint32_t rows, unsigned long long* err) const {
-    pb::Batch b;
-    b.rows = (int)rows; b.slots = d_slots; b.positions = d_positions; b.tokens = d_tokens;
-    b.hidden = hidden; b.aq = aq; b.ad = ad; b.asum = asum; b.q = q; b.k = k; b.v = v;
-    b.attn = attn; b.gate = gate; b.up = up; b.logits = logits; b.scores = scores;
-    b.score_stride = capacity + 4; b.kv = kv; b.capacity = capacity; b.history = history;
-    b.err = err;
-    return b;
-  }
-
-  // Enqueues one forward step for rows already staged in d_slots/d_positions/
-  // d_tokens; stage failures land in err[0..rows).
 #define PB_LAUNCH(cls, call) \
   do {                       \
     prof_mark(cls);          \
@@ -214,6 +206,49 @@ struct pb_engine {
     ++launches;              \
   } while (0)
 
+  pb::Batch batch(uint32_t rows, unsigned long long* err) const {
+    pb::Batch b;
+    b.rows = (int)rows; b.slots = d_slots; b.positions = d_positions; b.tokens = d_tokens;
+    b.hidden = hidden; b.aq = aq; b.ad = ad; b.asum = asum; b.q = q; b.k = k; b.v = v;
+    b.attn = attn; b.gate = gate; b.up = up; b.logits = logits; b.scores = scores;
+    b.score_stride = capacity + 4; b.kv = kv; b.capacity = capacity; b.history = history;
+    b.err = err;
+    if ((int)rows >= pb::kTcMinBatch) {
+      b.aq_tc = aq_tc; b.ad_tc = ad_tc; b.tc_seqs = tc_seqs;
+    }
+    return b;
+  }
+
+  // One matvec over the batch: the tensor-core path (tile image, up to three
+  // stacked matrices in one launch) from kTcMinBatch rows, else one CUDA-core
+  // matvec launch per matrix.
+  struct Mat {
+    const uint8_t* w;
+    int rows;
+    pb::Epilogue ep;
+  };
+  void matvec(int wtype, const pb::Batch& b, int columns, const uint8_t* tc_image,
+              std::initializer_list<Mat> mats, int cls) {
+    using namespace pb;
+    if (b.aq_tc) {
+      TcGemm g{};
+      g.wtype = wtype; g.tiles = tc_image; g.nb = columns / 32;
+      int rt = 0;
+      for (const Mat& m : mats) {
+        rt += m.rows / 128;
+        g.seg[g.nseg].rtile_end = rt;
+        g.seg[g.nseg].ep = m.ep;
+        ++g.nseg;
+      }
+      g.rtiles = rt;
+      PB_LAUNCH(cls, launch_tc_gemm(g, b, d_tc_status, stream));
+    } else {
+      for (const Mat& m : mats) PB_LAUNCH(cls, launch_qgemv(wtype, m.w, m.rows, columns, b, m.ep, stream));
+    }
+  }
+
+  // Enqueues one forward step for rows already staged in d_slots/d_positions/
+  // d_tokens; stage failures land in err[0..rows).
   void enqueue_forward(uint32_t rows, bool want_logits, unsigned long long* err) {
     using namespace pb;
     const pb_model* m = model;
@@ -225,40 +260,31 @@ struct pb_engine {
       auto T = [&](uint32_t role) { return m->tensor(layer_tensor(layer, role)); };
       PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(T(10)), ord,
                                                  D_ATTN_NORM, stream));
-      Epilogue ep{EPI_BIAS, q, kHidden, reinterpret_cast<const float*>(T(18)), err, ord, D_Q};
-      ep.tc_status = d_tc_status;
-      PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(19), 896, 896, b, ep, stream));
-      ep = {EPI_BIAS, k, 128, reinterpret_cast<const float*>(T(15)), err, ord, D_K};
-      ep.tc_status = d_tc_status;
-      PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(16), 128, 896, b, ep, stream));
-      ep = {EPI_BIAS, v, 128, reinterpret_cast<const float*>(T(20)), err, ord, D_V};
-      ep.tc_status = d_tc_status;
-      PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(21), 128, 896, b, ep, stream));
+      const Epilogue eq{EPI_BIAS, q, kHidden, reinterpret_cast<const float*>(T(18)), err, ord, D_Q};
+      const Epilogue ek{EPI_BIAS, k, 128, reinterpret_cast<const float*>(T(15)), err, ord, D_K};
+      const Epilogue ev{EPI_BIAS, v, 128, reinterpret_cast<const float*>(T(20)), err, ord, D_V};
+      matvec(W_Q4_0, b, 896, m->tc + m->tc_qkv[layer],
+             {{T(19), 896, eq}, {T(16), 128, ek}, {T(21), 128, ev}}, PB_KC_GEMV);
       PB_LAUNCH(PB_KC_ROPE_KV, launch_rope_kv(b, layer, m->rope, stream));
       PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, max_span, stream));
       PB_LAUNCH(PB_KC_QUANT, launch_quant(b, attn, kHidden, kHidden, stream));
-      ep = {EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_ATTN_OUTPUT};
-      ep.tc_status = d_tc_status;
-      PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(17), 896, 896, b, ep, stream));
+      const Epilogue eo{EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_ATTN_OUTPUT};
+      matvec(W_Q4_0, b, 896, m->tc + m->tc_o[layer], {{T(17), 896, eo}}, PB_KC_GEMV);
       PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(T(14)), ord,
                                                  D_FFN_NORM, stream));
-      ep = {EPI_STORE, gate, kFfn, nullptr, err, ord, D_GATE};
-      ep.tc_status = d_tc_status;
-      PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(12), 4864, 896, b, ep, stream));
-      ep = {EPI_STORE, up, kFfn, nullptr, err, ord, D_UP};
-      ep.tc_status = d_tc_status;
-      PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(13), 4864, 896, b, ep, stream));
+      const Epilogue eg{EPI_STORE, gate, kFfn, nullptr, err, ord, D_GATE};
+      const Epilogue eu{EPI_STORE, up, kFfn, nullptr, err, ord, D_UP};
+      matvec(W_Q4_0, b, 896, m->tc + m->tc_gateup[layer], {{T(12), 4864, eg}, {T(13), 4864, eu}},
+             PB_KC_GEMV);
       PB_LAUNCH(PB_KC_SWIGLU, launch_swiglu_quant(b, ord, stream));
-      ep = {EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_DOWN};
-      ep.tc_status = d_tc_status;
-      PB_LAUNCH(PB_KC_GEMV, launch_qgemv(W_Q4_0, T(11), 896, 4864, b, ep, stream));
+      const Epilogue ed{EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_DOWN};
+      matvec(W_Q4_0, b, 4864, m->tc + m->tc_down[layer], {{T(11), 896, ed}}, PB_KC_GEMV);
     }
     if (want_logits) {
       PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(m->tensor(289)),
                                                  25, D_OUTPUT_NORM, stream));
-      Epilogue ep{EPI_STORE, logits, (size_t)kVocab, nullptr, err, 25, D_LOGITS};
-      ep.tc_status = d_tc_status;
-      PB_LAUNCH(PB_KC_LM_HEAD, launch_qgemv(W_Q8_0, m->tensor(290), kVocab, 896, b, ep, stream));
+      const Epilogue el{EPI_STORE, logits, (size_t)kVocab, nullptr, err, 25, D_LOGITS};
+      matvec(W_Q8_0, b, 896, m->tc + m->tc_head, {{m->tensor(290), kVocab, el}}, PB_KC_LM_HEAD);
       PB_LAUNCH(PB_KC_ARGMAX, launch_argmax(logits, kVocab, rows, kVocab, d_greedy, d_greedy_bits,
                                             nullptr, stream));
     }
@@ -502,6 +528,9 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   chk(dalloc(&e->aq, S * 4864));
   chk(dalloc(&e->ad, S * 152));
   chk(dalloc(&e->asum, S * 152));
+  e->tc_seqs = (int)((S + 63) / 64 * 64);
+  chk(dalloc(&e->aq_tc, (size_t)e->tc_seqs * 4864));
+  chk(dalloc(&e->ad_tc, (size_t)e->tc_seqs * 152));
   chk(dalloc(&e->d_slots, S));
   chk(dalloc(&e->d_positions, S));
   chk(dalloc(&e->d_tokens, S));
@@ -526,6 +555,8 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   if (c == cudaSuccess) c = cudaMemset(e->kv, 0, S * (size_t)max_context * 6144 * 4);
   if (c == cudaSuccess) c = cudaMemset(e->history, 0, S * (size_t)max_context * 4);
   if (c == cudaSuccess) c = cudaMemset(e->d_tc_status, 0, 4);
+  if (c == cudaSuccess) c = cudaMemset(e->aq_tc, 0, (size_t)e->tc_seqs * 4864);
+  if (c == cudaSuccess) c = cudaMemset(e->ad_tc, 0, (size_t)e->tc_seqs * 152 * 4);
   if (c == cudaSuccess) *e->h_tc_status = 0;
   if (c != cudaSuccess) {
     pb::record_cuda_error(c, "pb_engine_create");
@@ -545,7 +576,7 @@ void pb_engine_destroy(pb_engine* e) {
                  e->logits, e->scores, e->aq, e->ad, e->asum, e->d_slots, e->d_positions,
                  e->d_tokens, e->d_err, e->d_greedy, e->d_greedy_bits, e->d_states,
                  e->d_hist_offset, e->d_hist_len, e->d_sampled, e->d_samp_status,
-                 e->d_token_log, e->d_tc_status};
+                 e->d_token_log, e->d_tc_status, e->aq_tc, e->ad_tc};
   for (void* p : dev) if (p) cudaFree(p);
   void* host[] = {e->h_slots, e->h_positions, e->h_tokens, e->h_err, e->h_greedy, e->h_greedy_bits,
                   e->h_tc_status};

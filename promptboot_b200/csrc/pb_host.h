@@ -46,6 +46,11 @@ struct pb_model {
   uint64_t offset[291] = {};         // file offsets of each tensor
   uint64_t length[291] = {};
   float* rope = nullptr;             // device RoPE table
+  // Tensor-core tile image of every matvec weight (pb_gemm_tc.cu layout), per
+  // layer [q|k|v] [o] [gate|up] [down] stacked by row tiles, then the output head.
+  uint8_t* tc = nullptr;
+  size_t tc_bytes = 0;
+  size_t tc_qkv[24] = {}, tc_o[24] = {}, tc_gateup[24] = {}, tc_down[24] = {}, tc_head = 0;
   const uint8_t* tensor(uint32_t id) const {
     return data + (offset[id] - pb::kTensorSection);
   }

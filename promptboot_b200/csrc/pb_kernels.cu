@@ -58,7 +58,8 @@ void launch_embed(const Batch& b, const uint8_t* embedding, cudaStream_t s) {
 // fp32_sse2.rs:945-983, one warp per 32-element block: d = amax / 127 rounded to
 // binary16 for storage, inverse from the unrounded d, q = trunc(x * inv +- 0.5).
 // The block's quant sum is kept for the Q4_0 zero-point correction.
-__device__ __forceinline__ void quantize_block_warp(float x, int8_t* aq, float* ad, int* asum) {
+__device__ __forceinline__ int quantize_block_warp(float x, int8_t* aq, float* ad, int* asum,
+                                                   float& dstored) {
   float amax = warp_max_f32(fbits(bitsf(x) & 0x7fffffffu));
   float d = __fdiv_rn(amax, 127.0f);
   float inverse = bitsf(d) == 0 ? 0.0f : __fdiv_rn(1.0f, d);
@@ -68,9 +69,26 @@ __device__ __forceinline__ void quantize_block_warp(float x, int8_t* aq, float* 
   int lane = threadIdx.x & 31;
   aq[lane] = (int8_t)q;
   int total = warp_sum_i32((int)(int8_t)q);
+  dstored = half_to_f32(f32_to_half(bitsf(d)));
   if (lane == 0) {
-    *ad = half_to_f32(f32_to_half(bitsf(d)));
+    *ad = dstored;
     *asum = total;
+  }
+  return q;
+}
+
+// Row `row`, block `blk` of a K = 32 * nb activation: quantizes into the
+// row-major buffers and, when the batch carries them, the tensor-core layout.
+__device__ __forceinline__ void quantize_row_block(const Batch& b, float x, int row, int blk, int nb) {
+  float d;
+  const int q = quantize_block_warp(x, b.aq + (size_t)row * kActStride + blk * 32,
+                                    b.ad + (size_t)row * kActBlocks + blk,
+                                    b.asum + (size_t)row * kActBlocks + blk, d);
+  if (b.aq_tc) {
+    const int lane = threadIdx.x & 31;
+    int8_t* t = b.aq_tc + ((size_t)(row >> 3) * nb + blk) * 256 + (row & 7) * 16;
+    t[(lane >> 4) * 128 + (lane & 15)] = (int8_t)q;
+    if (lane == 0) b.ad_tc[(size_t)blk * b.tc_seqs + row] = d;
   }
 }
 
@@ -111,9 +129,7 @@ __global__ void rmsnorm_quant_kernel(Batch b, const float* __restrict__ weight,
   }
   __syncthreads();
   for (int blk = warp; blk < kHidden / 32; blk += blockDim.x >> 5) {
-    quantize_block_warp(y[blk * 32 + lane], b.aq + (size_t)row * kActStride + blk * 32,
-                        b.ad + (size_t)row * kActBlocks + blk,
-                        b.asum + (size_t)row * kActBlocks + blk);
+    quantize_row_block(b, y[blk * 32 + lane], row, blk, kHidden / 32);
   }
 }
 
@@ -126,10 +142,7 @@ __global__ void quant_kernel(Batch b, const float* __restrict__ x, size_t ld, in
   int row = blockIdx.x;
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int blk = warp; blk < columns / 32; blk += blockDim.x >> 5) {
-    quantize_block_warp(x[(size_t)row * ld + blk * 32 + lane],
-                        b.aq + (size_t)row * kActStride + blk * 32,
-                        b.ad + (size_t)row * kActBlocks + blk,
-                        b.asum + (size_t)row * kActBlocks + blk);
+    quantize_row_block(b, x[(size_t)row * ld + blk * 32 + lane], row, blk, columns / 32);
   }
 }
 
@@ -152,9 +165,7 @@ __global__ void swiglu_quant_kernel(Batch b, uint32_t layer_ordinal) {
     float p = __fmul_rn(silu, u[e]);
     if (b.product_out) b.product_out[(size_t)row * kFfn + e] = p;
     check_finite(p, &b.err[row], layer_ordinal, D_SWIGLU, 0, e);
-    quantize_block_warp(p, b.aq + (size_t)row * kActStride + blk * 32,
-                        b.ad + (size_t)row * kActBlocks + blk,
-                        b.asum + (size_t)row * kActBlocks + blk);
+    quantize_row_block(b, p, row, blk, kFfn / 32);
   }
 }
 
@@ -265,10 +276,6 @@ static size_t qgemv_smem(int nb) {
 void launch_qgemv(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
                   const Epilogue& ep, cudaStream_t s) {
   const int nb = columns / 32;
-  if (ep.tc_status && qgemm_tc_supported(rows, b.rows, columns)) {
-    launch_qgemm_tc(wtype, w, rows, columns, b, ep, ep.tc_status, s);
-    return;
-  }
   if (wtype == W_Q4_0) {
     if (nb > 64) {
       constexpr int RT = 8;

@@ -38,6 +38,12 @@ struct Batch {
   float* product_out = nullptr;  // optional [B][4864] SwiGLU output (operator API)
   int span_min = 0;              // minimum softmax span (operator API; 0 = natural)
   float* probs_out = nullptr;    // optional [B][14][score_stride] final probabilities
+  // Tensor-core activation layout, written by the quantizers when aq_tc is set:
+  // quants [tc_seqs / 8][K / 32][256 B] (per 8 sequences and block: bytes 0-15
+  // of the 8 rows, then bytes 16-31), scales [K / 32][tc_seqs].
+  int8_t* aq_tc = nullptr;
+  float* ad_tc = nullptr;
+  int tc_seqs = 0;               // multiple of 64, >= rows
 };
 
 // Longest softmax span the shared-memory attention path holds; longer contexts
@@ -54,9 +60,6 @@ struct Epilogue {
   unsigned long long* err;
   uint32_t layer_ordinal;
   uint32_t domain;
-  // Device word the tensor-core path sets on a pipeline timeout; when null the
-  // CUDA-core matvec serves every batch size.
-  unsigned int* tc_status = nullptr;
 };
 
 enum WeightType : int { W_Q4_0 = 2, W_Q8_0 = 3 };
@@ -68,10 +71,38 @@ void launch_rmsnorm_quant(const Batch& b, const float* weight, uint32_t layer_or
 void launch_quant(const Batch& b, const float* x, size_t ld, int columns, cudaStream_t s);
 void launch_qgemv(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
                   const Epilogue& ep, cudaStream_t s);
-// tcgen05 kind::i8 path (pb_gemm_tc.cu) for batches above 8 rows.
-bool qgemm_tc_supported(int rows, int batch, int columns);
-void launch_qgemm_tc(int wtype, const uint8_t* w, int rows, int columns, const Batch& b,
-                     const Epilogue& ep, unsigned int* status, cudaStream_t s);
+
+// tcgen05 kind::i8 path (pb_gemm_tc.cu) for batches above 8 rows.  The weights
+// are read from a tile image (launch_tc_repack): per 128-row tile and chunk of
+// 4 Q-blocks, kTcChunkBytes = 4 canonical int8 tiles + 128 x 4 f32 scales.
+constexpr int kTcChunkBytes = 18432;
+constexpr int kTcMinBatch = 9;
+bool tc_shape_supported(int rows, int columns);
+size_t tc_image_bytes(int rows, int columns);
+void launch_tc_repack(int wtype, const uint8_t* w, int rows, int columns, uint8_t* out,
+                      cudaStream_t s);
+// Up to three matrices stacked by row tiles in one image and one launch (q/k/v,
+// gate/up); segment i covers row tiles [seg[i-1].rtile_end, seg[i].rtile_end)
+// and writes through its own epilogue with rows numbered from 0.
+struct TcSegment {
+  int rtile_end;
+  Epilogue ep;
+};
+struct TcGemm {
+  int wtype;
+  const uint8_t* tiles;
+  int rtiles;
+  int nb;  // Q-blocks per row (K / 32)
+  int nseg;
+  TcSegment seg[3];
+  // Bits of -0.0f, passed at run time: fl(a * b) is formed as fma(a, b, -0.0)
+  // with an addend the assembler cannot see, so it can never merge that product
+  // with the following accumulation into one fused operation.
+  uint32_t neg_zero_bits = 0x80000000u;
+};
+int tc_pick_tile(int rtiles, int batch);
+// Sets *status (device word) if a pipeline wait timed out.
+void launch_tc_gemm(const TcGemm& g, const Batch& b, unsigned int* status, cudaStream_t s);
 void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s);
 // max_span: the largest softmax span of the batch, (position + 4) & ~3 (or span_min).
 void launch_attention(const Batch& b, int layer, int max_span, cudaStream_t s);

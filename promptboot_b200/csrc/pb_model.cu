@@ -3,6 +3,8 @@
 // decode path), plus the library's host utilities: CUDA error capture, SHA-256
 // (FIPS 180-4) and the inference RoPE table.
 #include "pb_host.h"
+#include "pb_common.cuh"
+#include "pb_kernels.cuh"
 
 #include <cmath>
 
@@ -277,6 +279,50 @@ uint32_t validate_layout(const uint8_t* bytes, uint64_t len, pb_model_error* err
 
 }  // namespace
 
+namespace {
+
+// Builds the tensor-core tile image from the uploaded tensors (one repack launch
+// per matrix) and waits for it.
+cudaError_t build_tc_image(pb_model* m) {
+  using pb::launch_tc_repack;
+  using pb::tc_image_bytes;
+  auto lt = [](int layer, uint32_t role) { return 1u + (uint32_t)layer * 12u + (role - 10u); };
+  size_t off = 0;
+  for (int l = 0; l < pb::kLayers; ++l) {
+    m->tc_qkv[l] = off;
+    off += tc_image_bytes(896, 896) + 2 * tc_image_bytes(128, 896);
+    m->tc_o[l] = off;
+    off += tc_image_bytes(896, 896);
+    m->tc_gateup[l] = off;
+    off += 2 * tc_image_bytes(4864, 896);
+    m->tc_down[l] = off;
+    off += tc_image_bytes(896, 4864);
+  }
+  m->tc_head = off;
+  off += tc_image_bytes(pb::kVocab, 896);
+  m->tc_bytes = off;
+  cudaError_t e = cudaMalloc(&m->tc, off);
+  if (e != cudaSuccess) return e;
+  for (int l = 0; l < pb::kLayers; ++l) {
+    uint8_t* qkv = m->tc + m->tc_qkv[l];
+    launch_tc_repack(pb::W_Q4_0, m->tensor(lt(l, 19)), 896, 896, qkv, 0);
+    launch_tc_repack(pb::W_Q4_0, m->tensor(lt(l, 16)), 128, 896, qkv + tc_image_bytes(896, 896), 0);
+    launch_tc_repack(pb::W_Q4_0, m->tensor(lt(l, 21)), 128, 896,
+                     qkv + tc_image_bytes(896, 896) + tc_image_bytes(128, 896), 0);
+    launch_tc_repack(pb::W_Q4_0, m->tensor(lt(l, 17)), 896, 896, m->tc + m->tc_o[l], 0);
+    uint8_t* gu = m->tc + m->tc_gateup[l];
+    launch_tc_repack(pb::W_Q4_0, m->tensor(lt(l, 12)), 4864, 896, gu, 0);
+    launch_tc_repack(pb::W_Q4_0, m->tensor(lt(l, 13)), 4864, 896, gu + tc_image_bytes(4864, 896), 0);
+    launch_tc_repack(pb::W_Q4_0, m->tensor(lt(l, 11)), 896, 4864, m->tc + m->tc_down[l], 0);
+  }
+  launch_tc_repack(pb::W_Q8_0, m->tensor(290), pb::kVocab, 896, m->tc + m->tc_head, 0);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  return e;
+}
+
+}  // namespace
+
 extern "C" {
 
 uint32_t pb_abi_version(void) { return PB_ABI_VERSION; }
@@ -305,10 +351,12 @@ uint32_t pb_model_open(const uint8_t* bytes, uint64_t len, uint32_t flags, int d
                                        cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMalloc(&m->rope, rope.size() * 4);
   if (e == cudaSuccess) e = cudaMemcpy(m->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = build_tc_image(m);
   if (e != cudaSuccess) {
     pb::record_cuda_error(e, "pb_model_open");
     if (m->data) cudaFree(m->data);
     if (m->rope) cudaFree(m->rope);
+    if (m->tc) cudaFree(m->tc);
     delete m;
     return model_error(err, PB_DEVICE, 0, 0, 0, 0, (uint64_t)e, F_STATE_FIELD, 3);
   }
@@ -322,6 +370,7 @@ void pb_model_close(pb_model* model) {
   cudaSetDevice(model->device);
   if (model->data) cudaFree(model->data);
   if (model->rope) cudaFree(model->rope);
+  if (model->tc) cudaFree(model->tc);
   delete model;
 }
 

@@ -96,6 +96,30 @@ __global__ void iota_kernel(int* p, int n) {
   if (i < n) p[i] = i;
 }
 
+// Tensor-core operands of one operator call: the weight tile image and the
+// activation tile layout (zeroed, so padding sequences hold finite values).
+struct TcScratch {
+  uint8_t* image = nullptr;
+  int8_t* aq = nullptr;
+  float* ad = nullptr;
+  int seqs = 0;
+  cudaStream_t s;
+  explicit TcScratch(cudaStream_t st) : s(st) {}
+  cudaError_t alloc(size_t image_bytes, uint32_t rows, uint32_t cols) {
+    seqs = (int)((rows + 63) / 64 * 64);
+    cudaError_t e = cudaMallocAsync(&image, image_bytes, s);
+    if (!e) e = cudaMallocAsync(&aq, (size_t)seqs * cols, s);
+    if (!e) e = cudaMallocAsync(&ad, (size_t)seqs * (cols / 32) * 4, s);
+    if (!e) e = cudaMemsetAsync(aq, 0, (size_t)seqs * cols, s);
+    if (!e) e = cudaMemsetAsync(ad, 0, (size_t)seqs * (cols / 32) * 4, s);
+    return e;
+  }
+  ~TcScratch() {
+    void* p[] = {image, aq, ad};
+    for (void* x : p) if (x) cudaFreeAsync(x, s);
+  }
+};
+
 // Operator scratch: quantized activations, stage-error words, slot/position maps.
 struct OpScratch {
   int8_t* aq = nullptr;
@@ -233,11 +257,25 @@ uint32_t pb_qmatvec_device(uint32_t wtype, const uint8_t* w, uint32_t rows, uint
   OpScratch scr(s);
   PB_CUDA(scr.alloc(batch));
   pb::Batch b = scr.batch(batch);
-  pb::launch_quant(b, x, cols, (int)cols, s);
-  pb::Epilogue ep{pb::EPI_STORE, y, rows, nullptr, scr.err, 0, 0};
-  ep.tc_status = scr.tc_status;
-  pb::launch_qgemv((int)wtype, w, (int)rows, (int)cols, b, ep, s);
-  PB_CUDA(cudaGetLastError());
+  const pb::Epilogue ep{pb::EPI_STORE, y, rows, nullptr, scr.err, 0, 0};
+  if (batch >= (uint32_t)pb::kTcMinBatch && pb::tc_shape_supported((int)rows, (int)cols)) {
+    // Tensor-core path: tile image of w and the activation tile layout, built
+    // per call into stream-ordered scratch.
+    TcScratch tc(s);
+    PB_CUDA(tc.alloc(pb::tc_image_bytes((int)rows, (int)cols), batch, cols));
+    b.aq_tc = tc.aq; b.ad_tc = tc.ad; b.tc_seqs = tc.seqs;
+    pb::launch_tc_repack((int)wtype, w, (int)rows, (int)cols, tc.image, s);
+    pb::launch_quant(b, x, cols, (int)cols, s);
+    pb::TcGemm g{};
+    g.wtype = (int)wtype; g.tiles = tc.image; g.rtiles = (int)rows / 128; g.nb = (int)nb;
+    g.nseg = 1; g.seg[0].rtile_end = g.rtiles; g.seg[0].ep = ep;
+    pb::launch_tc_gemm(g, b, scr.tc_status, s);
+    PB_CUDA(cudaGetLastError());
+  } else {
+    pb::launch_quant(b, x, cols, (int)cols, s);
+    pb::launch_qgemv((int)wtype, w, (int)rows, (int)cols, b, ep, s);
+    PB_CUDA(cudaGetLastError());
+  }
   unsigned int status = 0;
   PB_CUDA(cudaMemcpyAsync(&status, scr.tc_status, 4, cudaMemcpyDeviceToHost, s));
   PB_CUDA(cudaStreamSynchronize(s));

@@ -221,6 +221,27 @@ def test_matvec_shapes_match_oracle(wtype, rows, cols, batch):
         assert np.array_equal(u32(got[b]), u32(ref)), b
 
 
+@pytest.mark.parametrize("tile", ["16", "32", "64"])
+@pytest.mark.parametrize("wtype,rows,cols,batch", [(2, 896, 4864, 100), (3, 1024, 896, 130),
+                                                   (2, 1152, 896, 64)])
+def test_tensor_core_every_tile_width(monkeypatch, tile, wtype, rows, cols, batch):
+    """Each sequence-tile width of the tcgen05 path (forced through PB_TC_TILE),
+    ragged last tiles included, equals the oracle bit for bit."""
+    monkeypatch.setenv("PB_TC_TILE", tile)
+    lib = _lib.load()
+    rng = np.random.default_rng(rows + batch + int(tile))
+    w = _q4_weights(rng, rows, cols) if wtype == 2 else _q8_weights(rng, rows, cols)
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    y = torch.zeros((batch, rows), dtype=torch.float32, device="cuda")
+    assert lib.pb_qmatvec_device(wtype, ptr(dev(w)), rows, cols, ptr(dev(x)), batch, ptr(y), None) == 0
+    sync()
+    got = host(y)
+    for b in range(batch):
+        st = oracle.prepare_q8(x[b])
+        ref = oracle.q4_matvec(w, st, rows, cols) if wtype == 2 else oracle.q8_matvec(w, st, rows, cols)
+        assert np.array_equal(u32(got[b]), u32(ref)), b
+
+
 def test_tensor_core_widest_tile_matches_oracle():
     """4864 x 896 Q4_0 at 512 rows: 16 sequence tiles per weight tile."""
     lib = _lib.load()
