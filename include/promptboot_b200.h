@@ -217,7 +217,8 @@ PB_API uint32_t pb_qmatvec_device_noalloc(uint32_t wtype, const uint8_t *w_devic
 /* Q8_0 staging in the reference's 34-byte block format for [rows][cols] f32. */
 PB_API uint32_t pb_quantize_q8_device(const float *x_device, uint32_t rows, uint32_t cols,
                                uint8_t *staging_device, void *stream);
-/* RMSNorm (fp32_sse2.rs:1310-1334) of [rows][896] into y. */
+/* RMSNorm (fp32_sse2.rs:1310-1334) of [rows][896] into y; x, w and y 16-byte
+ * aligned (PB_CAPACITY otherwise). */
 PB_API uint32_t pb_rmsnorm_device(const float *x_device, const float *w_device, uint32_t rows,
                            float *y_device, void *stream);
 /* SwiGLU (fp32_sse2.rs:1751-1770) of [rows][4864]. */

@@ -16,6 +16,7 @@
 // path serves contexts up to kAttnMaxPositions; longer ones use the per-head kernel.
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
+#include "pb_quant.cuh"
 
 namespace pb {
 namespace {
@@ -46,7 +47,7 @@ struct AttnSmem {
 };
 
 __global__ void __launch_bounds__(kThreads)
-attention_kv_group_kernel(Batch b, int layer, int span_cap) {
+attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize) {
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;
   float* buf0 = sm + AttnSmem::kQ;
@@ -169,13 +170,22 @@ attention_kv_group_kernel(Batch b, int layer, int span_cap) {
   const int qh = kh * kHeadsPerKv + h;
   b.attn[(size_t)row * kHidden + qh * 64 + lane64] = o;
   check_finite(o, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh * 64 + lane64);
+  if (quantize) {
+    // The group's 448 outputs are Q8_0 blocks 14 kh .. 14 kh + 13 of the
+    // o-projection input: stage them (q is no longer read) and quantize one
+    // block per warp.
+    qs[tid] = o;
+    __syncthreads();
+    const int w = tid >> 5;
+    quantize_row_block(b, qs[w * 32 + (tid & 31)], row, kh * kHeadsPerKv * 2 + w, kHidden / 32);
+  }
 }
 
 }  // namespace
 
 int attention_smem_positions() { return kAttnMaxPositions; }
 
-void launch_attention_grouped(const Batch& b, int layer, int span_cap, cudaStream_t s) {
+void launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, cudaStream_t s) {
   const size_t bytes = AttnSmem::bytes(span_cap);
   static size_t configured = 0;
   if (bytes > configured) {
@@ -183,7 +193,7 @@ void launch_attention_grouped(const Batch& b, int layer, int span_cap, cudaStrea
                          (int)AttnSmem::bytes(kAttnMaxPositions));
     configured = AttnSmem::bytes(kAttnMaxPositions);
   }
-  attention_kv_group_kernel<<<b.rows * 2, kThreads, bytes, s>>>(b, layer, span_cap);
+  attention_kv_group_kernel<<<b.rows * 2, kThreads, bytes, s>>>(b, layer, span_cap, quantize);
 }
 
 }  // namespace pb

@@ -249,7 +249,8 @@ struct pb_engine {
 
   // Enqueues one forward step for rows already staged in d_slots/d_positions/
   // d_tokens; stage failures land in err[0..rows).
-  void enqueue_forward(uint32_t rows, bool want_logits, unsigned long long* err) {
+  void enqueue_forward(uint32_t rows, bool want_logits, unsigned long long* err,
+                       bool want_greedy = true) {
     using namespace pb;
     const pb_model* m = model;
     Batch b = batch(rows, err);
@@ -266,8 +267,7 @@ struct pb_engine {
       matvec(W_Q4_0, b, 896, m->tc + m->tc_qkv[layer],
              {{T(19), 896, eq}, {T(16), 128, ek}, {T(21), 128, ev}}, PB_KC_GEMV);
       PB_LAUNCH(PB_KC_ROPE_KV, launch_rope_kv(b, layer, m->rope, stream));
-      PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, max_span, stream));
-      PB_LAUNCH(PB_KC_QUANT, launch_quant(b, attn, kHidden, kHidden, stream));
+      PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, max_span, true, stream));
       const Epilogue eo{EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_ATTN_OUTPUT};
       matvec(W_Q4_0, b, 896, m->tc + m->tc_o[layer], {{T(17), 896, eo}}, PB_KC_GEMV);
       PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(T(14)), ord,
@@ -285,8 +285,9 @@ struct pb_engine {
                                                  25, D_OUTPUT_NORM, stream));
       const Epilogue el{EPI_STORE, logits, (size_t)kVocab, nullptr, err, 25, D_LOGITS};
       matvec(W_Q8_0, b, 896, m->tc + m->tc_head, {{m->tensor(290), kVocab, el}}, PB_KC_LM_HEAD);
-      PB_LAUNCH(PB_KC_ARGMAX, launch_argmax(logits, kVocab, rows, kVocab, d_greedy, d_greedy_bits,
-                                            nullptr, stream));
+      if (want_greedy)
+        PB_LAUNCH(PB_KC_ARGMAX, launch_argmax(logits, kVocab, rows, kVocab, d_greedy, d_greedy_bits,
+                                              nullptr, stream));
     }
   }
 
@@ -888,7 +889,8 @@ uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
       for (uint32_t i = 0; i < n; ++i)
         e->max_span = std::max(e->max_span,
                                (int)((e->slots[seqs[i]].position + done + t + 4) & ~3u));
-      e->enqueue_forward(n, true, e->d_err + (size_t)t * n);
+      // Only the last step's greedy id is published (InferenceStep::selected).
+      e->enqueue_forward(n, true, e->d_err + (size_t)t * n, done + t + 1 == steps);
       increment_kernel<<<blocks, threads, 0, e->stream>>>(e->d_positions, (int)n);
       e->launches += 4;
     }

@@ -7,25 +7,13 @@
 // kernel, so that its binary32 results are the reference's bit for bit.
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
+#include "pb_quant.cuh"
 
 #include <cstdio>
 
 namespace pb {
 
 // ---------------------------------------------------------------- reductions
-
-__device__ __forceinline__ double warp_sum_f64(double v) {
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max_f32(float v) {
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-__device__ __forceinline__ int warp_sum_i32(int v) {
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
 
 // ------------------------------------------------------------------ embedding
 
@@ -53,89 +41,90 @@ void launch_embed(const Batch& b, const uint8_t* embedding, cudaStream_t s) {
   embed_kernel<<<b.rows, 128, 0, s>>>(b, embedding);
 }
 
-// ------------------------------------------------------------ Q8_0 quantizer
+// fp32_sse2.rs:1310-1334 then the quantizer.  The reference sums the 896 f64
+// squares serially.  Every square is a binary32 value, a multiple of the
+// smallest square's ulp u = 2^(emin - 150) (biased exponents, subnormals as 1);
+// all partial sums stay below 896 * 2^(emax - 126) < 2^(emax - 116), so when
+// emax - emin <= 19 every partial sum of any grouping is an f64-representable
+// multiple of u and the tree sum equals the serial one exactly.  Otherwise (or
+// with a non-finite square) one thread repeats the serial sum from shared memory.
+constexpr int kNormThreads = kHidden / 4;  // 224: one float4 per thread
 
-// fp32_sse2.rs:945-983, one warp per 32-element block: d = amax / 127 rounded to
-// binary16 for storage, inverse from the unrounded d, q = trunc(x * inv +- 0.5).
-// The block's quant sum is kept for the Q4_0 zero-point correction.
-__device__ __forceinline__ int quantize_block_warp(float x, int8_t* aq, float* ad, int* asum,
-                                                   float& dstored) {
-  float amax = warp_max_f32(fbits(bitsf(x) & 0x7fffffffu));
-  float d = __fdiv_rn(amax, 127.0f);
-  float inverse = bitsf(d) == 0 ? 0.0f : __fdiv_rn(1.0f, d);
-  float v = __fmul_rn(x, inverse);
-  float half = (bitsf(v) >> 31) == 0 ? 0.5f : -0.5f;
-  int q = __float2int_rz(__fadd_rn(v, half));
-  int lane = threadIdx.x & 31;
-  aq[lane] = (int8_t)q;
-  int total = warp_sum_i32((int)(int8_t)q);
-  dstored = half_to_f32(f32_to_half(bitsf(d)));
-  if (lane == 0) {
-    *ad = dstored;
-    *asum = total;
-  }
-  return q;
-}
-
-// Row `row`, block `blk` of a K = 32 * nb activation: quantizes into the
-// row-major buffers and, when the batch carries them, the tensor-core layout.
-__device__ __forceinline__ void quantize_row_block(const Batch& b, float x, int row, int blk, int nb) {
-  float d;
-  const int q = quantize_block_warp(x, b.aq + (size_t)row * kActStride + blk * 32,
-                                    b.ad + (size_t)row * kActBlocks + blk,
-                                    b.asum + (size_t)row * kActBlocks + blk, d);
-  if (b.aq_tc) {
-    const int lane = threadIdx.x & 31;
-    int8_t* t = b.aq_tc + ((size_t)(row >> 3) * nb + blk) * 256 + (row & 7) * 16;
-    t[(lane >> 4) * 128 + (lane & 15)] = (int8_t)q;
-    if (lane == 0) b.ad_tc[(size_t)blk * b.tc_seqs + row] = d;
-  }
-}
-
-// fp32_sse2.rs:1310-1334 then the quantizer.  The f64 sum of squares is reduced
-// across the block instead of in index order: the terms are binary32 squares
-// whose f64 sum is exact whenever their exponents lie within ~29 binades of the
-// largest; otherwise it differs from the serial sum by a few f64 ulps, which
-// changes the binary32 mean only when that lies within those ulps of a
-// binary32 rounding boundary (about 2^-27 per norm).
-__global__ void rmsnorm_quant_kernel(Batch b, const float* __restrict__ weight,
-                                     uint32_t layer_ordinal, uint32_t domain) {
-  __shared__ float y[kHidden];
-  __shared__ double partial[8];
-  int row = blockIdx.x;
-  const float* x = b.hidden + (size_t)row * kHidden;
+__global__ void __launch_bounds__(kNormThreads)
+rmsnorm_quant_kernel(Batch b, const float* __restrict__ weight, uint32_t layer_ordinal,
+                     uint32_t domain) {
+  __shared__ __align__(16) float sq[kHidden];  // squares, then the normalized row
+  __shared__ double part[kNormThreads / 32];
+  __shared__ int ext[2][kNormThreads / 32];
+  __shared__ double total;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int row = blockIdx.x;
+  const float4 xv = reinterpret_cast<const float4*>(b.hidden + (size_t)row * kHidden)[t];
+  const float4 wv = reinterpret_cast<const float4*>(weight)[t];
+  const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+  const float ws[4] = {wv.x, wv.y, wv.z, wv.w};
   double sum = 0.0;
-  for (int e = threadIdx.x; e < kHidden; e += blockDim.x) {
-    float v = x[e];
-    sum += (double)__fmul_rn(v, v);
+  int emin = 255, emax = 0;  // emax 255 marks a non-finite square
+  float q4[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float q = __fmul_rn(xs[i], xs[i]);
+    q4[i] = q;
+    sum += (double)q;
+    const uint32_t qb = bitsf(q) & 0x7fffffffu;
+    const int e = (int)(qb >> 23);
+    if (qb != 0) {
+      emin = min(emin, max(e, 1));
+      emax = max(emax, max(e, 1));
+    }
   }
+  *reinterpret_cast<float4*>(&sq[4 * t]) = make_float4(q4[0], q4[1], q4[2], q4[3]);
   sum = warp_sum_f64(sum);
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) partial[warp] = sum;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double t = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += partial[w];
-    partial[0] = t;
+  for (int o = 16; o > 0; o >>= 1) {
+    emin = min(emin, __shfl_xor_sync(0xffffffffu, emin, o));
+    emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
+  }
+  if (lane == 0) {
+    part[warp] = sum;
+    ext[0][warp] = emin;
+    ext[1][warp] = emax;
   }
   __syncthreads();
-  float mean = (float)(partial[0] / 896.0);
-  float inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, fbits(0x358637bdu))));
-  for (int e = threadIdx.x; e < kHidden; e += blockDim.x) {
-    float v = __fmul_rn(__fmul_rn(x[e], inverse), weight[e]);
-    y[e] = v;
-    if (b.norm_out) b.norm_out[(size_t)row * kHidden + e] = v;
-    check_finite(v, &b.err[row], layer_ordinal, domain, 0, e);
+  if (t == 0) {
+    double tree = 0.0;
+    int lo = 255, hi = 0;
+    for (int w = 0; w < kNormThreads / 32; ++w) {
+      tree += part[w];
+      lo = min(lo, ext[0][w]);
+      hi = max(hi, ext[1][w]);
+    }
+    if (hi == 255 || (hi >= lo && hi - lo > 19)) {
+      double serial = 0.0;
+      for (int e = 0; e < kHidden; ++e) serial += (double)sq[e];
+      tree = serial;
+    }
+    total = tree;
   }
   __syncthreads();
-  for (int blk = warp; blk < kHidden / 32; blk += blockDim.x >> 5) {
-    quantize_row_block(b, y[blk * 32 + lane], row, blk, kHidden / 32);
+  const float mean = (float)(total / 896.0);
+  const float inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, fbits(0x358637bdu))));
+  float y4[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    y4[i] = __fmul_rn(__fmul_rn(xs[i], inverse), ws[i]);
+    check_finite(y4[i], &b.err[row], layer_ordinal, domain, 0, 4 * t + i);
   }
+  const float4 yv = make_float4(y4[0], y4[1], y4[2], y4[3]);
+  *reinterpret_cast<float4*>(&sq[4 * t]) = yv;
+  if (b.norm_out) reinterpret_cast<float4*>(b.norm_out + (size_t)row * kHidden)[t] = yv;
+  __syncthreads();
+  for (int blk = warp; blk < kHidden / 32; blk += kNormThreads / 32)
+    quantize_row_block(b, sq[blk * 32 + lane], row, blk, kHidden / 32);
 }
 
 void launch_rmsnorm_quant(const Batch& b, const float* weight, uint32_t layer_ordinal,
                           uint32_t domain, cudaStream_t s) {
-  rmsnorm_quant_kernel<<<b.rows, 256, 0, s>>>(b, weight, layer_ordinal, domain);
+  rmsnorm_quant_kernel<<<b.rows, kNormThreads, 0, s>>>(b, weight, layer_ordinal, domain);
 }
 
 __global__ void quant_kernel(Batch b, const float* __restrict__ x, size_t ld, int columns) {
@@ -151,26 +140,43 @@ void launch_quant(const Batch& b, const float* x, size_t ld, int columns, cudaSt
 }
 
 // fp32_sse2.rs:1751-1770 then the quantizer: product = fl(fl(g / (1 + e)) * u)
-// with e = expf4(0 - g); checked as the SWIGLU stage.
-__global__ void swiglu_quant_kernel(Batch b, uint32_t layer_ordinal) {
-  int row = blockIdx.x;
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// with e = expf4(0 - g); checked as the SWIGLU stage.  Grid (rows, 4): each CTA
+// takes 38 of the 152 blocks, each warp loads all of its blocks before computing.
+constexpr int kSwigluSplit = 4;
+constexpr int kSwigluPerWarp = (kFfn / 32 / kSwigluSplit + 7) / 8;  // 5
+
+__global__ void __launch_bounds__(256) swiglu_quant_kernel(Batch b, uint32_t layer_ordinal) {
+  const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int blk0 = blockIdx.y * (kFfn / 32 / kSwigluSplit), blk_end = blk0 + kFfn / 32 / kSwigluSplit;
   const float* g = b.gate + (size_t)row * kFfn;
   const float* u = b.up + (size_t)row * kFfn;
-  for (int blk = warp; blk < kFfn / 32; blk += blockDim.x >> 5) {
-    int e = blk * 32 + lane;
-    float gv = g[e];
-    float ex = expf4_lane(__fsub_rn(0.0f, gv));
-    float silu = __fdiv_rn(gv, __fadd_rn(1.0f, ex));
-    float p = __fmul_rn(silu, u[e]);
-    if (b.product_out) b.product_out[(size_t)row * kFfn + e] = p;
-    check_finite(p, &b.err[row], layer_ordinal, D_SWIGLU, 0, e);
-    quantize_row_block(b, p, row, blk, kFfn / 32);
+  float gv[kSwigluPerWarp], uv[kSwigluPerWarp];
+#pragma unroll
+  for (int k = 0; k < kSwigluPerWarp; ++k) {
+    const int blk = blk0 + warp + 8 * k;
+    if (blk < blk_end) {
+      gv[k] = g[blk * 32 + lane];
+      uv[k] = u[blk * 32 + lane];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kSwigluPerWarp; ++k) {
+    const int blk = blk0 + warp + 8 * k;
+    if (blk < blk_end) {
+      const int e = blk * 32 + lane;
+      const float ex = expf4_lane(__fsub_rn(0.0f, gv[k]));
+      const float silu = __fdiv_rn(gv[k], __fadd_rn(1.0f, ex));
+      const float p = __fmul_rn(silu, uv[k]);
+      if (b.product_out) b.product_out[(size_t)row * kFfn + e] = p;
+      check_finite(p, &b.err[row], layer_ordinal, D_SWIGLU, 0, e);
+      quantize_row_block(b, p, row, blk, kFfn / 32);
+    }
   }
 }
 
 void launch_swiglu_quant(const Batch& b, uint32_t layer_ordinal, cudaStream_t s) {
-  swiglu_quant_kernel<<<b.rows, 256, 0, s>>>(b, layer_ordinal);
+  swiglu_quant_kernel<<<dim3(b.rows, kSwigluSplit), 256, 0, s>>>(b, layer_ordinal);
 }
 
 // ------------------------------------------------ block-scaled matvec (GEMV)
@@ -397,12 +403,13 @@ __global__ void attention_kernel(Batch b, int layer) {
   }
 }
 
-void launch_attention(const Batch& b, int layer, int max_span, cudaStream_t s) {
+void launch_attention(const Batch& b, int layer, int max_span, bool quantize, cudaStream_t s) {
   if (max_span <= kAttnMaxPositions) {
-    launch_attention_grouped(b, layer, (max_span + 3) & ~3, s);
+    launch_attention_grouped(b, layer, (max_span + 3) & ~3, quantize, s);
     return;
   }
   attention_kernel<<<b.rows * kQHeads, 256, 0, s>>>(b, layer);
+  if (quantize) launch_quant(b, b.attn, kHidden, kHidden, s);
 }
 
 // -------------------------------------------------------------- argmax/top8

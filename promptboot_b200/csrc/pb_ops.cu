@@ -301,7 +301,9 @@ uint32_t pb_quantize_q8_device(const float* x, uint32_t rows, uint32_t cols, uin
 }
 
 uint32_t pb_rmsnorm_device(const float* x, const float* w, uint32_t rows, float* y, void* stream) {
-  if (rows == 0) return PB_CAPACITY;
+  // The kernel moves each row as 224 float4 words.
+  auto aligned16 = [](const void* p) { return ((uintptr_t)p & 15u) == 0; };
+  if (rows == 0 || !aligned16(x) || !aligned16(w) || !aligned16(y)) return PB_CAPACITY;
   cudaStream_t s = (cudaStream_t)stream;
   OpScratch scr(s);
   PB_CUDA(scr.alloc(rows));
@@ -370,7 +372,7 @@ uint32_t pb_attention_device(const float* q, const float* kv, uint32_t capacity,
   b.q = const_cast<float*>(q); b.kv = const_cast<float*>(kv); b.capacity = capacity;
   b.attn = out; b.scores = sc; b.score_stride = span_max; b.span_min = (int)span;
   b.probs_out = scores;
-  pb::launch_attention(b, (int)layer, (int)span_max, s);
+  pb::launch_attention(b, (int)layer, (int)span_max, false, s);
   PB_CUDA(cudaGetLastError());
   if (!scores) PB_CUDA(cudaFreeAsync(sc, s));
   return PB_OK;

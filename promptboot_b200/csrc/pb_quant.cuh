@@ -1,0 +1,62 @@
+// Warp reductions and the Q8_0 activation quantizer shared by the kernels that
+// produce matvec inputs (RMSNorm, SwiGLU, attention output, the operator API).
+#pragma once
+
+#include "pb_common.cuh"
+#include "pb_kernels.cuh"
+
+namespace pb {
+
+__device__ __forceinline__ double warp_sum_f64(double v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max_f32(float v) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int warp_sum_i32(int v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ------------------------------------------------------------ Q8_0 quantizer
+
+// fp32_sse2.rs:945-983, one warp per 32-element block: d = amax / 127 rounded to
+// binary16 for storage, inverse from the unrounded d, q = trunc(x * inv +- 0.5).
+// The block's quant sum is kept for the Q4_0 zero-point correction.
+__device__ __forceinline__ int quantize_block_warp(float x, int8_t* aq, float* ad, int* asum,
+                                                   float& dstored) {
+  float amax = warp_max_f32(fbits(bitsf(x) & 0x7fffffffu));
+  float d = __fdiv_rn(amax, 127.0f);
+  float inverse = bitsf(d) == 0 ? 0.0f : __fdiv_rn(1.0f, d);
+  float v = __fmul_rn(x, inverse);
+  float half = (bitsf(v) >> 31) == 0 ? 0.5f : -0.5f;
+  int q = __float2int_rz(__fadd_rn(v, half));
+  int lane = threadIdx.x & 31;
+  aq[lane] = (int8_t)q;
+  int total = warp_sum_i32((int)(int8_t)q);
+  dstored = half_to_f32(f32_to_half(bitsf(d)));
+  if (lane == 0) {
+    *ad = dstored;
+    *asum = total;
+  }
+  return q;
+}
+
+// Row `row`, block `blk` of a K = 32 * nb activation: quantizes into the
+// row-major buffers and, when the batch carries them, the tensor-core layout.
+__device__ __forceinline__ void quantize_row_block(const Batch& b, float x, int row, int blk, int nb) {
+  float d;
+  const int q = quantize_block_warp(x, b.aq + (size_t)row * kActStride + blk * 32,
+                                    b.ad + (size_t)row * kActBlocks + blk,
+                                    b.asum + (size_t)row * kActBlocks + blk, d);
+  if (b.aq_tc) {
+    const int lane = threadIdx.x & 31;
+    int8_t* t = b.aq_tc + ((size_t)(row >> 3) * nb + blk) * 256 + (row & 7) * 16;
+    t[(lane >> 4) * 128 + (lane & 15)] = (int8_t)q;
+    if (lane == 0) b.ad_tc[(size_t)blk * b.tc_seqs + row] = d;
+  }
+}
+
+}  // namespace pb

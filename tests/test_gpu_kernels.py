@@ -65,6 +65,26 @@ def test_rmsnorm_matches_fixture_and_oracle():
         assert np.array_equal(u32(got[r]), u32(oracle.rmsnorm(xs[r], w)))
 
 
+def test_rmsnorm_wide_exponent_range_matches_oracle():
+    """Squares spanning more than 19 binades take the serial f64 sum (the
+    reference's order); narrow rows take the exact tree sum.  Both bit-exact."""
+    lib = _lib.load()
+    rng = np.random.default_rng(77)
+    rows = []
+    for lo, hi in [(-60, 20), (-30, 0), (-8, 2), (-1, 1), (-126, -100)]:
+        m = rng.uniform(1.0, 2.0, 896) * rng.choice([-1.0, 1.0], 896)
+        rows.append((m * np.exp2(rng.integers(lo, hi + 1, 896))).astype(np.float32))
+    rows[1][::7] = 0.0
+    xs = np.stack(rows)
+    w = rng.uniform(0.5, 1.5, 896).astype(np.float32)
+    y = torch.zeros((len(rows), 896), dtype=torch.float32, device="cuda")
+    assert lib.pb_rmsnorm_device(ptr(dev(xs)), ptr(dev(w)), len(rows), ptr(y), None) == 0
+    sync()
+    got = host(y)
+    for r in range(len(rows)):
+        assert np.array_equal(u32(got[r]), u32(oracle.rmsnorm(xs[r], w))), r
+
+
 def test_swiglu_matches_fixture_and_oracle():
     lib = _lib.load()
     g = np.array([((i % 33) - 16) / 16.0 for i in range(4864)], dtype=np.float32)
