@@ -3,17 +3,22 @@
 //
 // Arithmetic of the reference (sulewicz/promptboot fp32_sse2.rs:1430-1672), with
 // every order-sensitive f64 sum kept in the reference's order:
-//   score[h][p] = fl(f32(sum_c f64(fl(q[h][c] * k[p][c]))) * 0.125)  one thread per (h, p), c in order
+//   score[h][p] = fl(f32(sum_c f64(fl(q[h][c] * k[p][c]))) * 0.125)  c in order
 //   max over p (exact in any order)
 //   e = expf4(score - max), span padded to a multiple of 4 with e = 0
-//   sum = sum over 4-groups IN ORDER of f64(fl(fl(e0+e1) + fl(e2+e3)))   one thread per head
+//   sum = sum over 4-groups IN ORDER of f64(fl(fl(e0+e1) + fl(e2+e3)))   one lane per head
 //   prob = fl(e * f32(1.0 / sum))
-//   out[h][c] = f32(sum_p f64(fl(prob[h][p] * v[p][c])))              one thread per (h, c), p in order
-// K arrives in the reference's 4-position tiles and is transposed into shared
-// memory ([position][component], row pitch 65 words) so that a warp reading 32
-// positions at one component touches 32 banks; V tiles are row-major and are
-// streamed with cp.async double buffering.  Scores live in shared memory, so this
-// path serves contexts up to kAttnMaxPositions; longer ones use the per-head kernel.
+//   out[h][c] = f32(sum_p f64(fl(prob[h][p] * v[p][c])))              p in order
+// 224 threads = one warp per query head, so q and the probabilities are warp
+// broadcasts and the softmax needs no block barrier.  K arrives in the
+// reference's 4-position tiles ([component][4 positions], 1 KB) and is copied
+// untransposed by cp.async, 64 positions per chunk, into tiles padded to 260
+// words: lane (tile, pair) reads positions 4 tile + 2 pair + {0, 1} of one
+// component with one 8-byte load, and a half-warp covers all 32 banks once.
+// V chunks (row-major, 64 positions) reuse the two buffers.  Every lane keeps
+// two independent f64 chains (two positions in QK, components c and c + 32 in
+// PV).  Scores live in shared memory, so this path serves contexts up to
+// kAttnMaxPositions; longer ones use the per-head kernel.
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
 #include "pb_quant.cuh"
@@ -22,9 +27,9 @@ namespace pb {
 namespace {
 
 constexpr int kHeadsPerKv = 7;
-constexpr int kThreads = kHeadsPerKv * 64;  // 448
-constexpr int kTile = 64;                   // positions per K/V tile
-constexpr int kKPitch = 65;
+constexpr int kThreads = kHeadsPerKv * 32;  // 224
+constexpr int kChunk = 64;                  // positions per K/V chunk
+constexpr int kTilePitch = 260;             // words per padded 4-position K tile
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -37,147 +42,155 @@ __device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1
 __device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 struct AttnSmem {
-  static constexpr int kQ = (kHeadsPerKv * kKPitch + 3) & ~3;   // q, padded rows (16-B multiple)
-  static constexpr int kKBuf = kTile * kKPitch;                  // transposed K tile
-  static constexpr int kVBuf = kTile * 64;                       // V tile
+  static constexpr int kQ = kHeadsPerKv * 64;                 // q rows
+  static constexpr int kKBuf = (kChunk / 4) * kTilePitch;      // 16 padded K tiles
+  static constexpr int kVBuf = kChunk * 64;                    // V rows
   static constexpr int kBuf = kKBuf > kVBuf ? kKBuf : kVBuf;
   static size_t bytes(int span_cap) {
-    return (size_t)(kQ + 2 * kBuf + kHeadsPerKv * span_cap + 64) * 4;
+    return (size_t)(kQ + 2 * kBuf + kHeadsPerKv * span_cap) * 4;
   }
 };
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
 attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize) {
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;
-  float* buf0 = sm + AttnSmem::kQ;
-  float* buf1 = buf0 + AttnSmem::kBuf;
-  float* sc = buf1 + AttnSmem::kBuf;                   // [7][span_cap]
-  float* red = sc + kHeadsPerKv * span_cap;            // 64 words of scratch
-  float* bufs[2] = {buf0, buf1};
+  float* bufs[2] = {sm + AttnSmem::kQ, sm + AttnSmem::kQ + AttnSmem::kBuf};
+  float* sc = sm + AttnSmem::kQ + 2 * AttnSmem::kBuf;  // [7][span_cap]
 
   const int row = blockIdx.x >> 1, kh = blockIdx.x & 1;
-  const int tid = threadIdx.x;
-  const int h = tid >> 6, lane64 = tid & 63;
+  const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
   const int positions = b.positions[row] + 1;
   const int span = max((positions + 3) & ~3, b.span_min);
   const size_t cap = b.capacity;
   const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
   const float* kbase = kv + (size_t)layer * 4 * cap * 64 + (size_t)kh * (cap / 4) * 256;
   const float* vbase = kv + (size_t)layer * 4 * cap * 64 + 2 * cap * 64 + (size_t)kh * cap * 64;
-  const int ntiles = (positions + kTile - 1) / kTile;
+  const int nchunks = (positions + kChunk - 1) / kChunk;
+  const int ntiles = (positions + 3) >> 2;
+  float* score = sc + h * span_cap;
 
-  qs[h * kKPitch + lane64] = b.q[(size_t)row * kHidden + (kh * kHeadsPerKv + h) * 64 + lane64];
+  const float* qg = b.q + (size_t)row * kHidden + kh * kHeadsPerKv * 64;
+  qs[tid] = qg[tid];
+  qs[tid + kThreads] = qg[tid + kThreads];
 
-  // ---- scores: K tiles transposed into shared memory, one (head, position) per thread
-  // Tile t covers positions [64t, 64t + 64): the 16 4-position K tiles starting at
-  // word 256 * 16t of this head, i.e. 4096 contiguous words.
-  auto load_k = [&](int t, float (&reg)[10]) {
-    const int p0 = t * kTile;
-    const float* src = kbase + (size_t)p0 * 64;
-#pragma unroll
-    for (int i = 0; i < 10; ++i) {
-      const int wi = tid + i * kThreads;
-      const int p = p0 + (wi >> 8) * 4 + (wi & 3);
-      reg[i] = (wi < 4096 && p < positions) ? src[wi] : 0.0f;
-    }
-  };
-  auto store_k = [&](float* dst, const float (&reg)[10]) {
-#pragma unroll
-    for (int i = 0; i < 10; ++i) {
-      const int wi = tid + i * kThreads;
-      if (wi < 4096) dst[((wi >> 8) * 4 + (wi & 3)) * kKPitch + ((wi >> 2) & 63)] = reg[i];
-    }
-  };
-  float kreg[10];
-  load_k(0, kreg);
-  store_k(buf0, kreg);
-  __syncthreads();
-  for (int t = 0; t < ntiles; ++t) {
-    float* cur = bufs[t & 1];
-    if (t + 1 < ntiles) load_k(t + 1, kreg);  // global loads in flight during the dots
-    const int p = t * kTile + lane64;
-    if (p < positions) {
-      const float* kr = cur + lane64 * kKPitch;
-      const float* qr = qs + h * kKPitch;
-      double dot = 0.0;
-#pragma unroll 16
-      for (int c = 0; c < 64; ++c) dot += (double)__fmul_rn(qr[c], kr[c]);
-      sc[h * span_cap + p] = __fmul_rn((float)dot, 0.125f);
-    }
-    if (t + 1 < ntiles) store_k(bufs[(t + 1) & 1], kreg);
-    __syncthreads();
-  }
-
-  // ---- V tiles start streaming while the softmax runs
-  auto load_v = [&](int t, float* dst) {
-    const float* src = vbase + (size_t)t * kTile * 64;
-    const int rows_here = min(kTile, positions - t * kTile);
-    for (int i = tid; i < rows_here * 16; i += kThreads) cp_async16(dst + i * 4, src + i * 4);
+  // Chunk t = K tiles 16t .. 16t + 15, each 1 KB contiguous in the cache.
+  auto load_k = [&](int t, float* dst) {
+    const int tiles = min(kChunk / 4, ntiles - t * (kChunk / 4));
+    const float* src = kbase + (size_t)t * (kChunk / 4) * 256;
+    for (int i = tid; i < tiles * 64; i += kThreads)
+      cp_async16(dst + (i >> 6) * kTilePitch + (i & 63) * 4, src + i * 4);
     cp_commit();
   };
-  load_v(0, buf0);
-  if (ntiles > 1) load_v(1, buf1);
+  load_k(0, bufs[0]);
+  if (nchunks > 1) load_k(1, bufs[1]);
   else cp_commit();
 
-  // ---- max per head (exact in any order)
-  float m = fbits(0xff800000u);
-  for (int p = lane64; p < positions; p += 64) m = fmaxf(m, sc[h * span_cap + p]);
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((tid & 31) == 0) red[tid >> 5] = m;
-  __syncthreads();
-  const float maximum = fmaxf(red[2 * h], red[2 * h + 1]);
-
-  // ---- e = expf4(s - max), masked tail e = 0
-  for (int p = lane64; p < span; p += 64)
-    sc[h * span_cap + p] = p < positions ? expf4_lane(__fsub_rn(sc[h * span_cap + p], maximum)) : 0.0f;
-  __syncthreads();
-  // ---- f64 sum over 4-groups in order, one thread per head
-  if (lane64 == 0) {
-    const float* e = sc + h * span_cap;
-    double sum = 0.0;
-    for (int p = 0; p < span; p += 4)
-      sum += (double)__fadd_rn(__fadd_rn(e[p], e[p + 1]), __fadd_rn(e[p + 2], e[p + 3]));
-    red[16 + h] = (float)(1.0 / sum);
-  }
-  __syncthreads();
-  const float normalizer = red[16 + h];
-  for (int p = lane64; p < positions; p += 64)
-    sc[h * span_cap + p] = __fmul_rn(sc[h * span_cap + p], normalizer);
-  if (b.probs_out) {
-    float* dst = b.probs_out + ((size_t)row * kQHeads + kh * kHeadsPerKv + h) * b.score_stride;
-    for (int p = lane64; p < span; p += 64) dst[p] = sc[h * span_cap + p];
-  }
-
-  // ---- values: one (head, component) chain per thread, positions in order
-  double acc = 0.0;
-  const float* prob = sc + h * span_cap;
-  for (int t = 0; t < ntiles; ++t) {
+  // ---- scores: lane (tile, pair) -> positions 4 tile + 2 pair + {0, 1}
+  const int tile = lane >> 1, pair = lane & 1;
+  const float* qh = qs + h * 64;
+  for (int t = 0; t < nchunks; ++t) {
     cp_wait1();
     __syncthreads();
-    const float* vt = bufs[t & 1];
-    const int p0 = t * kTile;
-    const int rows_here = min(kTile, positions - p0);
-#pragma unroll 8
-    for (int i = 0; i < rows_here; ++i)
-      acc += (double)__fmul_rn(prob[p0 + i], vt[i * 64 + lane64]);
+    const float* kt = bufs[t & 1] + tile * kTilePitch + 2 * pair;
+    const int p = t * kChunk + 4 * tile + 2 * pair;
+    if (p < positions) {
+      double d0 = 0.0, d1 = 0.0;
+#pragma unroll 4
+      for (int c = 0; c < 64; c += 4) {
+        const float4 q4 = *reinterpret_cast<const float4*>(qh + c);
+        const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 k2 = *reinterpret_cast<const float2*>(kt + (c + j) * 4);
+          d0 += (double)__fmul_rn(qv[j], k2.x);
+          d1 += (double)__fmul_rn(qv[j], k2.y);
+        }
+      }
+      score[p] = __fmul_rn((float)d0, 0.125f);
+      if (p + 1 < positions) score[p + 1] = __fmul_rn((float)d1, 0.125f);
+    }
     __syncthreads();
-    if (t + 2 < ntiles) load_v(t + 2, bufs[t & 1]);
+    if (t + 2 < nchunks) load_k(t + 2, bufs[t & 1]);
     else cp_commit();
   }
   cp_wait0();
-  const float o = (float)acc;
-  const int qh = kh * kHeadsPerKv + h;
-  b.attn[(size_t)row * kHidden + qh * 64 + lane64] = o;
-  check_finite(o, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh * 64 + lane64);
-  if (quantize) {
-    // The group's 448 outputs are Q8_0 blocks 14 kh .. 14 kh + 13 of the
-    // o-projection input: stage them (q is no longer read) and quantize one
-    // block per warp.
-    qs[tid] = o;
+  __syncthreads();
+
+  // ---- V chunks start streaming while the softmax runs
+  auto load_v = [&](int t, float* dst) {
+    const float* src = vbase + (size_t)t * kChunk * 64;
+    const int rows_here = min(kChunk, positions - t * kChunk);
+    for (int i = tid; i < rows_here * 16; i += kThreads) cp_async16(dst + i * 4, src + i * 4);
+    cp_commit();
+  };
+  load_v(0, bufs[0]);
+  if (nchunks > 1) load_v(1, bufs[1]);
+  else cp_commit();
+
+  // ---- softmax of head h, entirely within warp h
+  float m = fbits(0xff800000u);
+  for (int p = lane; p < positions; p += 32) m = fmaxf(m, score[p]);
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  for (int p = lane; p < span; p += 32)
+    score[p] = p < positions ? expf4_lane(__fsub_rn(score[p], m)) : 0.0f;
+  __syncwarp();
+  float normalizer = 0.0f;
+  if (lane == 0) {
+    double sum = 0.0;
+    for (int p = 0; p < span; p += 4) {
+      const float4 e = *reinterpret_cast<const float4*>(score + p);
+      sum += (double)__fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
+    }
+    normalizer = (float)(1.0 / sum);
+  }
+  normalizer = __shfl_sync(0xffffffffu, normalizer, 0);
+  for (int p = lane; p < positions; p += 32) score[p] = __fmul_rn(score[p], normalizer);
+  __syncwarp();
+  if (b.probs_out) {
+    float* dst = b.probs_out + ((size_t)row * kQHeads + kh * kHeadsPerKv + h) * b.score_stride;
+    for (int p = lane; p < span; p += 32) dst[p] = score[p];
+  }
+
+  // ---- values: lane owns components lane and lane + 32 of head h, positions in order
+  double acc0 = 0.0, acc1 = 0.0;
+  for (int t = 0; t < nchunks; ++t) {
+    cp_wait1();
     __syncthreads();
-    const int w = tid >> 5;
-    quantize_row_block(b, qs[w * 32 + (tid & 31)], row, kh * kHeadsPerKv * 2 + w, kHidden / 32);
+    const float* vt = bufs[t & 1];
+    const float* pr = score + t * kChunk;
+    const int rows_here = min(kChunk, positions - t * kChunk);
+    int i = 0;
+    for (; i + 4 <= rows_here; i += 4) {
+      const float4 p4 = *reinterpret_cast<const float4*>(pr + i);
+      const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc0 += (double)__fmul_rn(pv[j], vt[(i + j) * 64 + lane]);
+        acc1 += (double)__fmul_rn(pv[j], vt[(i + j) * 64 + lane + 32]);
+      }
+    }
+    for (; i < rows_here; ++i) {
+      acc0 += (double)__fmul_rn(pr[i], vt[i * 64 + lane]);
+      acc1 += (double)__fmul_rn(pr[i], vt[i * 64 + lane + 32]);
+    }
+    __syncthreads();
+    if (t + 2 < nchunks) load_v(t + 2, bufs[t & 1]);
+    else cp_commit();
+  }
+  cp_wait0();
+  const float o0 = (float)acc0, o1 = (float)acc1;
+  const int qh_index = kh * kHeadsPerKv + h;
+  float* out = b.attn + (size_t)row * kHidden + qh_index * 64;
+  out[lane] = o0;
+  out[lane + 32] = o1;
+  check_finite(o0, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + lane);
+  check_finite(o1, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + lane + 32);
+  if (quantize) {
+    // Head qh's 64 outputs are Q8_0 blocks 2 qh and 2 qh + 1 of the
+    // o-projection input, one value per lane each.
+    quantize_row_block(b, o0, row, 2 * qh_index, kHidden / 32);
+    quantize_row_block(b, o1, row, 2 * qh_index + 1, kHidden / 32);
   }
 }
 
@@ -187,7 +200,7 @@ int attention_smem_positions() { return kAttnMaxPositions; }
 
 void launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, cudaStream_t s) {
   const size_t bytes = AttnSmem::bytes(span_cap);
-  static size_t configured = 0;
+  static size_t configured = 0;  // one device per process
   if (bytes > configured) {
     cudaFuncSetAttribute(attention_kv_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)AttnSmem::bytes(kAttnMaxPositions));
