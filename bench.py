@@ -265,7 +265,9 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
+        torch.cuda.nvtx.range_push("pb_timed")  # ncu --nvtx --nvtx-include pb_timed/
         st, _, errs = eng.generate(seqs, states, args.steps, want_tokens=False)
+        torch.cuda.nvtx.range_pop()
         e1.record(stream)
         torch.cuda.synchronize()
         barrier(world)

@@ -189,8 +189,8 @@ attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize) {
   if (quantize) {
     // Head qh's 64 outputs are Q8_0 blocks 2 qh and 2 qh + 1 of the
     // o-projection input, one value per lane each.
-    quantize_row_block(b, o0, row, 2 * qh_index, kHidden / 32);
-    quantize_row_block(b, o1, row, 2 * qh_index + 1, kHidden / 32);
+    quantize_row_block(b, o0, row, 2 * qh_index);
+    quantize_row_block(b, o1, row, 2 * qh_index + 1);
   }
 }
 

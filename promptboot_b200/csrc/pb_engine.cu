@@ -135,7 +135,6 @@ struct pb_engine {
   float* ad = nullptr;
   int* asum = nullptr;
   int8_t* aq_tc = nullptr;  // tensor-core activation layout (pb_kernels.cuh Batch)
-  float* ad_tc = nullptr;
   int tc_seqs = 0;
   int *d_slots = nullptr, *d_positions = nullptr;
   uint32_t* d_tokens = nullptr;
@@ -214,7 +213,7 @@ struct pb_engine {
     b.score_stride = capacity + 4; b.kv = kv; b.capacity = capacity; b.history = history;
     b.err = err;
     if ((int)rows >= pb::kTcMinBatch) {
-      b.aq_tc = aq_tc; b.ad_tc = ad_tc; b.tc_seqs = tc_seqs;
+      b.aq_tc = aq_tc; b.tc_seqs = tc_seqs;
     }
     return b;
   }
@@ -530,8 +529,7 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   chk(dalloc(&e->ad, S * 152));
   chk(dalloc(&e->asum, S * 152));
   e->tc_seqs = (int)((S + 63) / 64 * 64);
-  chk(dalloc(&e->aq_tc, (size_t)e->tc_seqs * 4864));
-  chk(dalloc(&e->ad_tc, (size_t)e->tc_seqs * 152));
+  chk(dalloc(&e->aq_tc, pb::tc_act_bytes(e->tc_seqs, 4864)));
   chk(dalloc(&e->d_slots, S));
   chk(dalloc(&e->d_positions, S));
   chk(dalloc(&e->d_tokens, S));
@@ -556,8 +554,7 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   if (c == cudaSuccess) c = cudaMemset(e->kv, 0, S * (size_t)max_context * 6144 * 4);
   if (c == cudaSuccess) c = cudaMemset(e->history, 0, S * (size_t)max_context * 4);
   if (c == cudaSuccess) c = cudaMemset(e->d_tc_status, 0, 4);
-  if (c == cudaSuccess) c = cudaMemset(e->aq_tc, 0, (size_t)e->tc_seqs * 4864);
-  if (c == cudaSuccess) c = cudaMemset(e->ad_tc, 0, (size_t)e->tc_seqs * 152 * 4);
+  if (c == cudaSuccess) c = cudaMemset(e->aq_tc, 0, pb::tc_act_bytes(e->tc_seqs, 4864));
   if (c == cudaSuccess) *e->h_tc_status = 0;
   if (c != cudaSuccess) {
     pb::record_cuda_error(c, "pb_engine_create");
@@ -577,7 +574,7 @@ void pb_engine_destroy(pb_engine* e) {
                  e->logits, e->scores, e->aq, e->ad, e->asum, e->d_slots, e->d_positions,
                  e->d_tokens, e->d_err, e->d_greedy, e->d_greedy_bits, e->d_states,
                  e->d_hist_offset, e->d_hist_len, e->d_sampled, e->d_samp_status,
-                 e->d_token_log, e->d_tc_status, e->aq_tc, e->ad_tc};
+                 e->d_token_log, e->d_tc_status, e->aq_tc};
   for (void* p : dev) if (p) cudaFree(p);
   void* host[] = {e->h_slots, e->h_positions, e->h_tokens, e->h_err, e->h_greedy, e->h_greedy_bits,
                   e->h_tc_status};

@@ -8,10 +8,12 @@
 //    canonical K-major int8 tiles (Q4_0 nibbles already shifted to q - 8, Q8_0
 //    quants as stored) followed by the 128 x 4 binary32 block scales;
 //  * the activation TILE LAYOUT written by the Q8_0 quantizers beside the
-//    row-major one: quants as [seq / 8][block][256 B] (two 8 x 16-byte core
-//    matrices per block) and scales as [block][seq].
-// So every chunk arrives with 1 + NT/8 + 4 bulk copies (cp.async.bulk, no
-// multicast) on one transaction-count mbarrier, issued by one thread.
+//    row-major one, chunk-major: per chunk and 8 sequences, 4 blocks x 256 B
+//    of quants (two 8 x 16-byte core matrices per block) then their
+//    [4 blocks][8 sequences] binary32 scales (1152 B, the B operand's 8-row
+//    group stride).
+// So every chunk arrives with two bulk copies (cp.async.bulk, no multicast) on
+// one transaction-count mbarrier, issued by one thread.
 //
 // One tcgen05.mma per Q-block: M = 128 weight rows, N = NT sequences, K = 32,
 // both operands signed.  TMEM columns are preloaded with 0x4B400000 and the MMA
@@ -37,6 +39,7 @@
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
 
+#include <algorithm>
 #include <cstdlib>
 
 namespace pb {
@@ -146,19 +149,34 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Waits for the phase of `bar` with the given parity.  Gives up when another
-// role has aborted, or after 200 ms (then aborts every role); false = give up.
-__device__ __noinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
+// Slow path of wait_phase: polls with a 20 us suspend hint; gives up when
+// another role has aborted, or after 200 ms (then aborts every role).
+__device__ __noinline__ bool wait_phase_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const uint64_t deadline = global_ns() + 200000000ull;
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_suspend(bar, parity)) return true;
     if (*abort_flag) return false;
     if (global_ns() > deadline) {
       *abort_flag = 1;
       return false;
     }
   }
+}
+// Waits for the phase of `bar` with the given parity; false = give up.
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return wait_phase_slow(bar, parity, abort_flag);
 }
 // wait_phase for a whole warp: every lane gets the same answer, so the warp
 // never splits around the .sync.aligned instructions that follow.
@@ -209,31 +227,97 @@ constexpr int kDwOff = kKC * kATile;
 constexpr uint32_t kMagic = 0x4B400000u;  // binary32 1.5 * 2^23
 static_assert(kDwOff + kM * kKC * 4 == kTcChunkBytes, "tile image chunk size");
 
-template <int NT>
+// Kernel configurations: NT sequences per tile, CPW TMEM columns per epilogue
+// warp (4 lane quarters x NT / CPW column groups), PER_SM resident CTAs per SM
+// (shared memory, TMEM columns and registers sized for that count), STAGES ring
+// depth.  Wide tiles for many tiles per SM, narrow tiles with many epilogue
+// warps when there are about as many tiles as SMs (latency-bound).
+template <int NT_, int CPW_, int PER_SM_, int STAGES_, int GROUPS_>
 struct TcCfg {
-  static constexpr int kEpiWarps = NT / 4;  // 4 lane quarters x NT/16 column groups
+  static constexpr int NT = NT_;
+  static constexpr int kCpw = CPW_;
+  static constexpr int kEpiWarps = 4 * NT / kCpw;
   static constexpr int kThreads = (2 + kEpiWarps) * 32;
-  static constexpr int kStages = NT == 64 ? 6 : 4;
-  static constexpr int kBOff = kTcChunkBytes;          // [NT/8][4 blocks][256 B]
-  static constexpr int kDaOff = kBOff + NT * 128;      // [4 blocks][NT] f32
-  static constexpr int kStage = kDaOff + NT * 16;
+  static constexpr int kPerSm = PER_SM_;
+  static constexpr int kStages = STAGES_;
+  // TMEM groups of 4 block dots: the MMA runs up to kGroups - 1 chunks ahead of
+  // the epilogue, hiding the MMA issue-to-commit latency.
+  static constexpr int kGroups = GROUPS_;
+  // Q-blocks per TMEM load batch (32 registers of block dots per thread).
+  static constexpr int kBatch = kCpw * kKC <= 16 ? kKC : 2;
+  static constexpr int kBOff = kTcChunkBytes;  // [NT/8] groups of kTcGroupBytes
+  static constexpr int kStage = kBOff + (NT / 8) * kTcGroupBytes;
   static constexpr int kBarOff = kStages * kStage;
-  static constexpr int kBytes = kBarOff + (2 * kStages + 4) * 8 + 16;
-  static constexpr uint32_t kCols = 2 * kKC * NT;      // two TMEM groups of 4 blocks
+  static constexpr int kBytes = kBarOff + (2 * kStages + 2 * kGroups) * 8 + 16;
+  static constexpr uint32_t kCols = kGroups * kKC * NT;
   static_assert(kStage % 128 == 0, "stage alignment");
+  static_assert(kCpw == 4 || kCpw == 8 || kCpw == 16, "epilogue column batch");
+  static_assert(kThreads <= 1024, "block size");
+  static_assert(kPerSm * kCols <= 512, "TMEM columns per SM");
+  static_assert((kCols & (kCols - 1)) == 0 && kCols >= 32, "TMEM allocation size");
+  static_assert(kPerSm * (kBytes + 1024) <= 233472, "shared memory per SM");
 };
+using CfgLatency = TcCfg<16, 4, 1, 6, 8>;   // 16 epilogue warps, one CTA per SM
+using Cfg16 = TcCfg<16, 8, 2, 4, 4>;
+using Cfg32 = TcCfg<32, 16, 2, 4, 2>;
+using Cfg64 = TcCfg<64, 16, 1, 6, 2>;
 
-template <bool Q4, int NT>
-__global__ void __launch_bounds__(TcCfg<NT>::kThreads, NT == 64 ? 1 : 2)
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&v)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld_cols<16>(uint32_t taddr, uint32_t (&v)[16]) {
+  tmem_ld16(taddr, v);
+}
+template <>
+__device__ __forceinline__ void tmem_ld_cols<8>(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                 "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_ld_cols<4>(uint32_t taddr, uint32_t (&v)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(taddr)
+               : "memory");
+}
+template <int N>
+__device__ __forceinline__ void tmem_st_same(uint32_t taddr, uint32_t x);
+template <>
+__device__ __forceinline__ void tmem_st_same<4>(uint32_t taddr, uint32_t x) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%1,%1,%1};" ::"r"(taddr), "r"(x)
+               : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st_same<16>(uint32_t taddr, uint32_t x) {
+  tmem_st16_same(taddr, x);
+}
+template <>
+__device__ __forceinline__ void tmem_st_same<8>(uint32_t taddr, uint32_t x) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+               "r"(x)
+               : "memory");
+}
+
+// Persistent: CTA i serves tiles i, i + G, i + 2G, ... (G = gridDim.x) of the
+// (row tile, sequence tile) grid, sequence tile fastest, so CTAs running at the
+// same time share weight tiles in L2; the ring, the MMA issue and the TMEM
+// groups run on one chunk counter across tile boundaries.
+template <bool Q4, class C>
+__global__ void __launch_bounds__(C::kThreads, C::kPerSm)
 qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
-  using C = TcCfg<NT>;
+  constexpr int NT = C::NT;
   constexpr int S = C::kStages;
+  constexpr int CPW = C::kCpw;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);  // stage landed
   uint64_t* empty = full + S;                                         // stage drained
-  uint64_t* tfull = empty + S;                                        // TMEM group ready [2]
-  uint64_t* tempty = tfull + 2;                                       // TMEM group drained [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  constexpr int G = C::kGroups;
+  uint64_t* tfull = empty + S;                                        // TMEM group ready [G]
+  uint64_t* tempty = tfull + G;                                       // TMEM group drained [G]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + G);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   // kind::i8 instruction descriptor: s32 accumulator, A and B signed, K-major,
@@ -242,10 +326,9 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
       (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int seq0 = blockIdx.x * NT;
-  const int rt = blockIdx.y;
-  const int nseq = min(NT, b.rows - seq0);
   const int nchunks = g.nb / kKC;
+  const int nst = (b.rows + NT - 1) / NT;  // sequence tiles
+  const int ntiles = g.rtiles * nst;
   const int quarter = warp & 3, cg = (warp - 2) >> 2;  // epilogue warps only
 
   if (warp == 0) tmem_alloc(tmem_slot, C::kCols);
@@ -254,7 +337,7 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
       mbar_init(&full[st], 1);
       mbar_init(&empty[st], C::kEpiWarps);
     }
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < G; ++k) {
       mbar_init(&tfull[k], 1);
       mbar_init(&tempty[k], C::kEpiWarps);
     }
@@ -265,61 +348,66 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
   __syncthreads();
   tc_after_sync();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tlane = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(cg * 16);
+  const uint32_t tlane = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(cg * CPW);
   if (warp >= 2) {
 #pragma unroll
-    for (int k = 0; k < 2 * kKC; ++k) tmem_st16_same(tlane + (uint32_t)(k * NT), kMagic);
+    for (int k = 0; k < G * kKC; ++k) tmem_st_same<CPW>(tlane + (uint32_t)(k * NT), kMagic);
     tmem_wait_st();
   }
   tc_before_sync();
   __syncthreads();
   tc_after_sync();
 
-  uint64_t acc[8];  // epilogue: 16 columns as 8 packed pairs
-#pragma unroll
-  for (int p = 0; p < 8; ++p) acc[p] = 0;
   int mma_last = -1;
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint8_t* wt = g.tiles + (size_t)rt * nchunks * kTcChunkBytes;
-      const int8_t* bq = b.aq_tc + (size_t)(seq0 >> 3) * g.nb * 256;
-      const float* da = b.ad_tc + seq0;
-      int load_last = -1;
-      for (int c = 0; c < nchunks; ++c) {
-        const int st = c % S;
-        if (!wait_phase(&empty[st], ((c / S) & 1) ^ 1, abort_flag)) break;
-        uint8_t* sp = smem + st * C::kStage;
-        mbar_expect_tx(&full[st], C::kStage);
-        bulk_g2s(sp, wt + (size_t)c * kTcChunkBytes, kTcChunkBytes, &full[st]);
-#pragma unroll
-        for (int rg = 0; rg < NT / 8; ++rg)
-          bulk_g2s(sp + C::kBOff + rg * 1024, bq + ((size_t)rg * g.nb + c * kKC) * 256, 1024, &full[st]);
-#pragma unroll
-        for (int j = 0; j < kKC; ++j)
-          bulk_g2s(sp + C::kDaOff + j * NT * 4, da + (size_t)(c * kKC + j) * b.tc_seqs, NT * 4,
-                   &full[st]);
-        load_last = c;
+      int q = 0, load_last = -1;
+      bool stop = false;
+      for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
+        const int rt = tile / nst, seq0 = (tile % nst) * NT;
+        const uint8_t* wt = g.tiles + (size_t)rt * nchunks * kTcChunkBytes;
+        for (int c = 0; c < nchunks; ++c, ++q) {
+          const int st = q % S;
+          if (!wait_phase(&empty[st], ((q / S) & 1) ^ 1, abort_flag)) {
+            stop = true;
+            break;
+          }
+          uint8_t* sp = smem + st * C::kStage;
+          mbar_expect_tx(&full[st], C::kStage);
+          bulk_g2s(sp, wt + (size_t)c * kTcChunkBytes, kTcChunkBytes, &full[st]);
+          bulk_g2s(sp + C::kBOff,
+                   b.aq_tc + ((size_t)c * (b.tc_seqs >> 3) + (seq0 >> 3)) * kTcGroupBytes,
+                   (NT / 8) * kTcGroupBytes, &full[st]);
+          load_last = q;
+        }
       }
       // Every issued copy lands before the CTA may exit.
-      for (int c = max(0, load_last - S + 1); c <= load_last; ++c)
-        wait_drain(&full[c % S], (c / S) & 1, 50000000ull);
+      for (int k = max(0, load_last - S + 1); k <= load_last; ++k)
+        wait_drain(&full[k % S], (k / S) & 1, 50000000ull);
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
-      for (int c = 0; c < nchunks; ++c) {
-        const int gr = c & 1, st = c % S, k2 = c >> 1;
-        if (!wait_phase(&tempty[gr], (k2 & 1) ^ 1, abort_flag)) break;
-        if (!wait_phase(&full[st], (c / S) & 1, abort_flag)) break;
-        tc_after_sync();
-        const uint8_t* sp = smem + st * C::kStage;
+      int q = 0;
+      bool stop = false;
+      for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
+        for (int c = 0; c < nchunks; ++c, ++q) {
+          const int gr = q % G, st = q % S, k2 = q / G;
+          if (!wait_phase(&tempty[gr], (k2 & 1) ^ 1, abort_flag) ||
+              !wait_phase(&full[st], (q / S) & 1, abort_flag)) {
+            stop = true;
+            break;
+          }
+          tc_after_sync();
+          const uint8_t* sp = smem + st * C::kStage;
 #pragma unroll
-        for (int j = 0; j < kKC; ++j)
-          mma_i8_acc(tmem_base + (uint32_t)((gr * kKC + j) * NT), smem_desc(sp + j * kATile, 256),
-                     smem_desc(sp + C::kBOff + j * 256, 1024), kIdesc);
-        mma_commit(&tfull[gr]);
-        mma_last = c;
+          for (int j = 0; j < kKC; ++j)
+            mma_i8_acc(tmem_base + (uint32_t)((gr * kKC + j) * NT), smem_desc(sp + j * kATile, 256),
+                       smem_desc(sp + C::kBOff + j * 256, kTcGroupBytes), kIdesc);
+          mma_commit(&tfull[gr]);
+          mma_last = q;
+        }
       }
     }
     __syncwarp();
@@ -328,57 +416,97 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
     const uint64_t neg_magic2 = pk(-12582912.0f, -12582912.0f);
     const float nz = __uint_as_float(g.neg_zero_bits);
     const uint64_t z2 = pk(nz, nz);
-    for (int c = 0; c < nchunks; ++c) {
-      const int gr = c & 1, st = c % S, k2 = c >> 1;
-      if (!wait_warp(&tfull[gr], k2 & 1, abort_flag)) break;
-      if (!wait_warp(&full[st], (c / S) & 1, abort_flag)) break;
-      tc_after_sync();
-      const uint8_t* sp = smem + st * C::kStage;
-      const float4 dw4 = *reinterpret_cast<const float4*>(sp + kDwOff + lrow * 16);
-      const float dw[kKC] = {dw4.x, dw4.y, dw4.z, dw4.w};
-      const uint32_t tg = tlane + (uint32_t)(gr * kKC * NT);
-      const float* dA = reinterpret_cast<const float*>(sp + C::kDaOff) + cg * 16;
-      // Two blocks per TMEM batch keeps the live registers low; every
-      // (row, sequence) still adds its blocks in order j = 0, 1, 2, 3.
+    int q = 0;
+    bool stop = false;
+    for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
+      uint64_t acc[CPW / 2];
 #pragma unroll
-      for (int jb = 0; jb < kKC; jb += 2) {
-        uint32_t v[2][16];
-        tmem_ld16(tg + (uint32_t)(jb * NT), v[0]);
-        tmem_ld16(tg + (uint32_t)((jb + 1) * NT), v[1]);
-        tmem_wait_ld();
-        tmem_st16_same(tg + (uint32_t)(jb * NT), kMagic);
-        tmem_st16_same(tg + (uint32_t)((jb + 1) * NT), kMagic);
-        uint64_t w2[2], n2[2];
-#pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          w2[jj] = pk(dw[jb + jj], dw[jb + jj]);
-          const float nm = -__fmul_rn(12582912.0f, dw[jb + jj]);
-          n2[jj] = pk(nm, nm);
+      for (int p = 0; p < CPW / 2; ++p) acc[p] = 0;
+      for (int c = 0; c < nchunks; ++c, ++q) {
+        const int gr = q % G, st = q % S, k2 = q / G;
+        if (!wait_warp(&tfull[gr], k2 & 1, abort_flag) || !wait_warp(&full[st], (q / S) & 1, abort_flag)) {
+          stop = true;
+          break;
         }
+        tc_after_sync();
+        const uint8_t* sp = smem + st * C::kStage;
+        const float4 dw4 = *reinterpret_cast<const float4*>(sp + kDwOff + lrow * 16);
+        const float dw[kKC] = {dw4.x, dw4.y, dw4.z, dw4.w};
+        const uint32_t tg = tlane + (uint32_t)(gr * kKC * NT);
+        // dA of (block j, column s): group s / 8, float 256 + 8 j + s % 8.
+        const int s0 = cg * CPW;
+        // kBatch blocks per TMEM load batch; every (row, sequence) still adds
+        // its blocks in order j = 0, 1, 2, 3.
+        constexpr int BT = C::kBatch;
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          uint64_t a = acc[p];
+        for (int jb = 0; jb < kKC; jb += BT) {
+          uint32_t v[BT][CPW];
 #pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            const uint64_t da2 = *reinterpret_cast<const uint64_t*>(dA + (jb + jj) * NT + 2 * p);
-            const uint64_t x2 = pk_u(v[jj][2 * p], v[jj][2 * p + 1]);
-            uint64_t t;
-            if (Q4) {
-              t = fma2(fma2(x2, w2[jj], n2[jj]), da2, z2);
-            } else {
-              t = fma2(add2(x2, neg_magic2), mul2(w2[jj], da2), z2);
-            }
-            a = add2(a, t);
+          for (int jj = 0; jj < BT; ++jj) tmem_ld_cols<CPW>(tg + (uint32_t)((jb + jj) * NT), v[jj]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int jj = 0; jj < BT; ++jj) tmem_st_same<CPW>(tg + (uint32_t)((jb + jj) * NT), kMagic);
+          uint64_t w2[BT], n2[BT];
+#pragma unroll
+          for (int jj = 0; jj < BT; ++jj) {
+            w2[jj] = pk(dw[jb + jj], dw[jb + jj]);
+            const float nm = -__fmul_rn(12582912.0f, dw[jb + jj]);
+            n2[jj] = pk(nm, nm);
           }
-          acc[p] = a;
+#pragma unroll
+          for (int p = 0; p < CPW / 2; ++p) {
+            uint64_t a = acc[p];
+#pragma unroll
+            for (int jj = 0; jj < BT; ++jj) {
+              const int s = s0 + 2 * p;
+              const uint64_t da2 = *reinterpret_cast<const uint64_t*>(
+                  sp + C::kBOff + (s >> 3) * kTcGroupBytes + 1024 + ((jb + jj) * 8 + (s & 7)) * 4);
+              const uint64_t x2 = pk_u(v[jj][2 * p], v[jj][2 * p + 1]);
+              uint64_t t;
+              if (Q4) {
+                t = fma2(fma2(x2, w2[jj], n2[jj]), da2, z2);
+              } else {
+                t = fma2(add2(x2, neg_magic2), mul2(w2[jj], da2), z2);
+              }
+              a = add2(a, t);
+            }
+            acc[p] = a;
+          }
+        }
+        tmem_wait_st();
+        tc_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&tempty[gr]);
+          mbar_arrive(&empty[st]);
         }
       }
-      tmem_wait_st();
-      tc_before_sync();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&tempty[gr]);
-        mbar_arrive(&empty[st]);
+      if (stop) break;
+      // Tile done: epilogue stores for rows of this warp's lane quarter.
+      const int rt = tile / nst, seq0 = (tile % nst) * NT;
+      const int nseq = min(NT, b.rows - seq0);
+      int si = 0;
+      while (si + 1 < g.nseg && rt >= g.seg[si].rtile_end) ++si;
+      const Epilogue& ep = g.seg[si].ep;
+      const int row = (rt - (si ? g.seg[si - 1].rtile_end : 0)) * kM + lrow;
+#pragma unroll
+      for (int p = 0; p < CPW / 2; ++p) {
+        float pair[2];
+        unpk(acc[p], pair[0], pair[1]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int s = cg * CPW + 2 * p + h;
+          if (s < nseq) {
+            const int seq = seq0 + s;
+            float* dst = ep.out + (size_t)seq * ep.ld + row;
+            float y;
+            if (ep.mode == EPI_BIAS) y = __fadd_rn(pair[h], ep.bias[row]);
+            else if (ep.mode == EPI_RESIDUAL) y = __fadd_rn(*dst, pair[h]);
+            else y = pair[h];
+            *dst = y;
+            check_finite(y, &ep.err[seq], ep.layer_ordinal, ep.domain, 0, row);
+          }
+        }
       }
     }
   }
@@ -386,49 +514,24 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
   __syncthreads();
   const bool aborted = *abort_flag != 0;
   if (aborted && warp == 1 && lane == 0 && mma_last >= 0)
-    wait_drain(&tfull[mma_last & 1], (mma_last >> 1) & 1, 50000000ull);  // committed MMAs finish
+    wait_drain(&tfull[mma_last % G], (mma_last / G) & 1, 50000000ull);  // committed MMAs finish
   if (aborted && tid == 0) atomicOr(status, 1u);
   tc_before_sync();
   __syncthreads();
   tc_after_sync();
   if (warp == 0) tmem_dealloc(tmem_base, C::kCols);
-  if (aborted || warp < 2) return;
-
-  int si = 0;
-  while (si + 1 < g.nseg && rt >= g.seg[si].rtile_end) ++si;
-  const Epilogue& ep = g.seg[si].ep;
-  const int row = (rt - (si ? g.seg[si - 1].rtile_end : 0)) * kM + quarter * 32 + lane;
-#pragma unroll
-  for (int p = 0; p < 8; ++p) {
-    float pair[2];
-    unpk(acc[p], pair[0], pair[1]);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int s = cg * 16 + 2 * p + h;
-      if (s < nseq) {
-        const int seq = seq0 + s;
-        float* dst = ep.out + (size_t)seq * ep.ld + row;
-        float y;
-        if (ep.mode == EPI_BIAS) y = __fadd_rn(pair[h], ep.bias[row]);
-        else if (ep.mode == EPI_RESIDUAL) y = __fadd_rn(*dst, pair[h]);
-        else y = pair[h];
-        *dst = y;
-        check_finite(y, &ep.err[seq], ep.layer_ordinal, ep.domain, 0, row);
-      }
-    }
-  }
 }
 
-template <bool Q4, int NT>
-void launch_tc(const TcGemm& g, const Batch& b, unsigned int* status, cudaStream_t s) {
-  using C = TcCfg<NT>;
+template <bool Q4, class C>
+void launch_tc(const TcGemm& g, const Batch& b, unsigned int* status, cudaStream_t s, int sms) {
   static bool configured = false;  // one device per process
   if (!configured) {
-    cudaFuncSetAttribute(qgemm_tc_kernel<Q4, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kBytes);
+    cudaFuncSetAttribute(qgemm_tc_kernel<Q4, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kBytes);
     configured = true;
   }
-  dim3 grid((b.rows + NT - 1) / NT, g.rtiles);
-  qgemm_tc_kernel<Q4, NT><<<grid, C::kThreads, C::kBytes, s>>>(g, b, status);
+  const int tiles = g.rtiles * ((b.rows + C::NT - 1) / C::NT);
+  const int grid = std::min(tiles, sms * C::kPerSm);
+  qgemm_tc_kernel<Q4, C><<<grid, C::kThreads, C::kBytes, s>>>(g, b, status);
 }
 
 // Tile image of one matrix: grid (chunks, row tiles), thread = row of the tile.
@@ -472,50 +575,63 @@ void launch_tc_repack(int wtype, const uint8_t* w, int rows, int columns, uint8_
   else tc_repack_kernel<34><<<grid, kM, 0, s>>>(w, nb, out);
 }
 
-// Picks the sequence tile NT (16, 32 or 64 sequences) with the smallest
-// estimated time: tile waves over the SM slots the tile's TMEM and shared
-// memory allow, times the per-tile epilogue work (grows with NT) plus a fixed
-// per-tile cost.  The weight row tile is the slow grid dimension so the CTAs
-// sharing it run together (one HBM read).  PB_TC_TILE=16|32|64 in the
-// environment forces a width (tests cover every width; tuning sweeps).
-int tc_pick_tile(int rtiles, int batch) {
-  if (const char* f = std::getenv("PB_TC_TILE")) {
-    const int nt = std::atoi(f);
-    if (nt == 16 || nt == 32 || nt == 64) return nt;
-  }
-  static const int kSms = [] {
-    int dev = 0, n = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    return n;
+namespace {
+int sm_count() {
+  static const int n = [] {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
   }();
+  return n;
+}
+}  // namespace
+
+// Configuration choice: 0 CfgLatency, 1 Cfg16, 2 Cfg32, 3 Cfg64.  With no
+// more tiles than SMs the latency configuration (most epilogue warps per tile)
+// wins; otherwise the one with the smallest busiest-CTA tile count times
+// per-tile epilogue work per SM slot.  PB_TC_TILE=L|16|32|64 in the environment
+// forces one (tests cover every configuration; tuning sweeps).
+int tc_pick_config(int rtiles, int batch) {
+  if (const char* f = std::getenv("PB_TC_TILE")) {
+    if (f[0] == 'L') return 0;
+    const int nt = std::atoi(f);
+    if (nt == 16) return 1;
+    if (nt == 32) return 2;
+    if (nt == 64) return 3;
+  }
+  const int sms = sm_count();
+  if ((long)rtiles * ((batch + 15) / 16) <= sms) return 0;
   const int nts[3] = {64, 32, 16};
-  const int per_sm[3] = {1, 2, 2};
-  int best = 16;
+  const int per_sm[3] = {Cfg64::kPerSm, Cfg32::kPerSm, Cfg16::kPerSm};
+  const int ids[3] = {3, 2, 1};
+  int best = 1;
   double best_cost = 1e30;
   for (int i = 0; i < 3; ++i) {
-    const int nt = nts[i];
-    const long tiles = (long)rtiles * ((batch + nt - 1) / nt);
-    const long slots = (long)kSms * per_sm[i];
-    const long waves = (tiles + slots - 1) / slots;
-    const double cost = (double)waves * (nt + 16) / per_sm[i];
+    const long tiles = (long)rtiles * ((batch + nts[i] - 1) / nts[i]);
+    const long slots = (long)sms * per_sm[i];
+    const long busiest = (tiles + slots - 1) / slots;
+    const double cost = (double)busiest * nts[i] / per_sm[i];
     if (cost < best_cost) {
       best_cost = cost;
-      best = nt;
+      best = ids[i];
     }
   }
   return best;
 }
 
 void launch_tc_gemm(const TcGemm& g, const Batch& b, unsigned int* status, cudaStream_t s) {
-  const int nt = tc_pick_tile(g.rtiles, b.rows);
+  const int cfg = tc_pick_config(g.rtiles, b.rows);
+  const int sms = sm_count();
   if (g.wtype == W_Q4_0) {
-    if (nt == 64) launch_tc<true, 64>(g, b, status, s);
-    else if (nt == 32) launch_tc<true, 32>(g, b, status, s);
-    else launch_tc<true, 16>(g, b, status, s);
+    if (cfg == 0) launch_tc<true, CfgLatency>(g, b, status, s, sms);
+    else if (cfg == 1) launch_tc<true, Cfg16>(g, b, status, s, sms);
+    else if (cfg == 2) launch_tc<true, Cfg32>(g, b, status, s, sms);
+    else launch_tc<true, Cfg64>(g, b, status, s, sms);
   } else {
-    if (nt == 64) launch_tc<false, 64>(g, b, status, s);
-    else if (nt == 32) launch_tc<false, 32>(g, b, status, s);
-    else launch_tc<false, 16>(g, b, status, s);
+    if (cfg == 0) launch_tc<false, CfgLatency>(g, b, status, s, sms);
+    else if (cfg == 1) launch_tc<false, Cfg16>(g, b, status, s, sms);
+    else if (cfg == 2) launch_tc<false, Cfg32>(g, b, status, s, sms);
+    else launch_tc<false, Cfg64>(g, b, status, s, sms);
   }
 }
 

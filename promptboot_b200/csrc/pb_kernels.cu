@@ -119,7 +119,7 @@ rmsnorm_quant_kernel(Batch b, const float* __restrict__ weight, uint32_t layer_o
   if (b.norm_out) reinterpret_cast<float4*>(b.norm_out + (size_t)row * kHidden)[t] = yv;
   __syncthreads();
   for (int blk = warp; blk < kHidden / 32; blk += kNormThreads / 32)
-    quantize_row_block(b, sq[blk * 32 + lane], row, blk, kHidden / 32);
+    quantize_row_block(b, sq[blk * 32 + lane], row, blk);
 }
 
 void launch_rmsnorm_quant(const Batch& b, const float* weight, uint32_t layer_ordinal,
@@ -131,7 +131,7 @@ __global__ void quant_kernel(Batch b, const float* __restrict__ x, size_t ld, in
   int row = blockIdx.x;
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int blk = warp; blk < columns / 32; blk += blockDim.x >> 5) {
-    quantize_row_block(b, x[(size_t)row * ld + blk * 32 + lane], row, blk, columns / 32);
+    quantize_row_block(b, x[(size_t)row * ld + blk * 32 + lane], row, blk);
   }
 }
 
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(Batch b, uint32_t lay
       const float p = __fmul_rn(silu, uv[k]);
       if (b.product_out) b.product_out[(size_t)row * kFfn + e] = p;
       check_finite(p, &b.err[row], layer_ordinal, D_SWIGLU, 0, e);
-      quantize_row_block(b, p, row, blk, kFfn / 32);
+      quantize_row_block(b, p, row, blk);
     }
   }
 }

@@ -38,11 +38,12 @@ struct Batch {
   float* product_out = nullptr;  // optional [B][4864] SwiGLU output (operator API)
   int span_min = 0;              // minimum softmax span (operator API; 0 = natural)
   float* probs_out = nullptr;    // optional [B][14][score_stride] final probabilities
-  // Tensor-core activation layout, written by the quantizers when aq_tc is set:
-  // quants [tc_seqs / 8][K / 32][256 B] (per 8 sequences and block: bytes 0-15
-  // of the 8 rows, then bytes 16-31), scales [K / 32][tc_seqs].
+  // Tensor-core activation layout, written by the quantizers when aq_tc is set,
+  // chunk-major (4 Q-blocks per chunk) so one chunk of one sequence tile is one
+  // contiguous copy: [K / 128][tc_seqs / 8][kTcGroupBytes], each 8-sequence
+  // group = 4 blocks x 256 B of quants (bytes 0-15 of the 8 rows, then bytes
+  // 16-31) followed by the [4 blocks][8 sequences] binary32 scales.
   int8_t* aq_tc = nullptr;
-  float* ad_tc = nullptr;
   int tc_seqs = 0;               // multiple of 64, >= rows
 };
 
@@ -76,6 +77,11 @@ void launch_qgemv(int wtype, const uint8_t* w, int rows, int columns, const Batc
 // are read from a tile image (launch_tc_repack): per 128-row tile and chunk of
 // 4 Q-blocks, kTcChunkBytes = 4 canonical int8 tiles + 128 x 4 f32 scales.
 constexpr int kTcChunkBytes = 18432;
+constexpr int kTcGroupBytes = 4 * 256 + 4 * 8 * 4;  // 1152
+// Bytes of the tensor-core activation layout for tc_seqs sequences and K columns.
+constexpr size_t tc_act_bytes(int tc_seqs, int columns) {
+  return (size_t)(columns / 128) * (tc_seqs / 8) * kTcGroupBytes;
+}
 constexpr int kTcMinBatch = 9;
 bool tc_shape_supported(int rows, int columns);
 size_t tc_image_bytes(int rows, int columns);
@@ -100,7 +106,7 @@ struct TcGemm {
   // with the following accumulation into one fused operation.
   uint32_t neg_zero_bits = 0x80000000u;
 };
-int tc_pick_tile(int rtiles, int batch);
+int tc_pick_config(int rtiles, int batch);
 // Sets *status (device word) if a pipeline wait timed out.
 void launch_tc_gemm(const TcGemm& g, const Batch& b, unsigned int* status, cudaStream_t s);
 void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s);

@@ -101,21 +101,19 @@ __global__ void iota_kernel(int* p, int n) {
 struct TcScratch {
   uint8_t* image = nullptr;
   int8_t* aq = nullptr;
-  float* ad = nullptr;
   int seqs = 0;
   cudaStream_t s;
   explicit TcScratch(cudaStream_t st) : s(st) {}
   cudaError_t alloc(size_t image_bytes, uint32_t rows, uint32_t cols) {
     seqs = (int)((rows + 63) / 64 * 64);
+    const size_t act = pb::tc_act_bytes(seqs, (int)cols);
     cudaError_t e = cudaMallocAsync(&image, image_bytes, s);
-    if (!e) e = cudaMallocAsync(&aq, (size_t)seqs * cols, s);
-    if (!e) e = cudaMallocAsync(&ad, (size_t)seqs * (cols / 32) * 4, s);
-    if (!e) e = cudaMemsetAsync(aq, 0, (size_t)seqs * cols, s);
-    if (!e) e = cudaMemsetAsync(ad, 0, (size_t)seqs * (cols / 32) * 4, s);
+    if (!e) e = cudaMallocAsync(&aq, act, s);
+    if (!e) e = cudaMemsetAsync(aq, 0, act, s);
     return e;
   }
   ~TcScratch() {
-    void* p[] = {image, aq, ad};
+    void* p[] = {image, aq};
     for (void* x : p) if (x) cudaFreeAsync(x, s);
   }
 };
@@ -263,7 +261,7 @@ uint32_t pb_qmatvec_device(uint32_t wtype, const uint8_t* w, uint32_t rows, uint
     // per call into stream-ordered scratch.
     TcScratch tc(s);
     PB_CUDA(tc.alloc(pb::tc_image_bytes((int)rows, (int)cols), batch, cols));
-    b.aq_tc = tc.aq; b.ad_tc = tc.ad; b.tc_seqs = tc.seqs;
+    b.aq_tc = tc.aq; b.tc_seqs = tc.seqs;
     pb::launch_tc_repack((int)wtype, w, (int)rows, (int)cols, tc.image, s);
     pb::launch_quant(b, x, cols, (int)cols, s);
     pb::TcGemm g{};

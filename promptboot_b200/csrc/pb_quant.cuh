@@ -46,16 +46,19 @@ __device__ __forceinline__ int quantize_block_warp(float x, int8_t* aq, float* a
 
 // Row `row`, block `blk` of a K = 32 * nb activation: quantizes into the
 // row-major buffers and, when the batch carries them, the tensor-core layout.
-__device__ __forceinline__ void quantize_row_block(const Batch& b, float x, int row, int blk, int nb) {
+__device__ __forceinline__ void quantize_row_block(const Batch& b, float x, int row, int blk) {
   float d;
   const int q = quantize_block_warp(x, b.aq + (size_t)row * kActStride + blk * 32,
                                     b.ad + (size_t)row * kActBlocks + blk,
                                     b.asum + (size_t)row * kActBlocks + blk, d);
   if (b.aq_tc) {
+    // Chunk-major tensor-core layout (Batch::aq_tc): group (blk / 4, row / 8),
+    // quants of block blk % 4 at 256 (blk % 4), its scales after the 4 blocks.
     const int lane = threadIdx.x & 31;
-    int8_t* t = b.aq_tc + ((size_t)(row >> 3) * nb + blk) * 256 + (row & 7) * 16;
-    t[(lane >> 4) * 128 + (lane & 15)] = (int8_t)q;
-    if (lane == 0) b.ad_tc[(size_t)blk * b.tc_seqs + row] = d;
+    const int j = blk & 3;
+    int8_t* grp = b.aq_tc + ((size_t)(blk >> 2) * (b.tc_seqs >> 3) + (row >> 3)) * kTcGroupBytes;
+    grp[j * 256 + (lane >> 4) * 128 + (row & 7) * 16 + (lane & 15)] = (int8_t)q;
+    if (lane == 0) reinterpret_cast<float*>(grp + 1024)[j * 8 + (row & 7)] = d;
   }
 }
 
