@@ -53,6 +53,7 @@ struct AttnSmem {
 
 __global__ void __launch_bounds__(kThreads, 4)
 attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize) {
+  pdl_begin();
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;
   float* bufs[2] = {sm + AttnSmem::kQ, sm + AttnSmem::kQ + AttnSmem::kBuf};
@@ -206,7 +207,7 @@ void launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quan
                          (int)AttnSmem::bytes(kAttnMaxPositions));
     configured = AttnSmem::bytes(kAttnMaxPositions);
   }
-  attention_kv_group_kernel<<<b.rows * 2, kThreads, bytes, s>>>(b, layer, span_cap, quantize);
+  launch_pdl(attention_kv_group_kernel, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
 }
 
 }  // namespace pb

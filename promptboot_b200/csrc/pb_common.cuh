@@ -33,6 +33,15 @@ enum Domain : uint32_t {
   D_SWIGLU = 15, D_DOWN = 16, D_OUTPUT_NORM = 17, D_LOGITS = 18,
 };
 
+// Programmatic dependent launch: every forward kernel starts with this.  It
+// lets the next kernel of the stream be scheduled while this one runs (its
+// CTAs then wait here), and waits until the previous kernel has completed and
+// its memory is visible, before any global memory is read or written.  A
+// no-op for kernels launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.launch_dependents;\n\tgriddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ float fbits(uint32_t b) { return __uint_as_float(b); }
 __device__ __forceinline__ uint32_t bitsf(float f) { return __float_as_uint(f); }
 __device__ __forceinline__ bool finite_bits(uint32_t b) {

@@ -93,6 +93,7 @@ cudaError_t dalloc(T** p, size_t count) {
 
 __global__ void advance_kernel(const pb::SamplerRow* sampled, uint32_t* tokens, int* positions,
                                uint32_t* token_log, int n) {
+  pb::pdl_begin();
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   uint32_t id = sampled[i].selected;
@@ -101,12 +102,14 @@ __global__ void advance_kernel(const pb::SamplerRow* sampled, uint32_t* tokens, 
 }
 
 __global__ void increment_kernel(int* positions, int n) {
+  pb::pdl_begin();
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) positions[i] += 1;
 }
 
 __global__ void record_sampler_status(const pb::SamplerRow* sampled, unsigned long long* status_log,
                                       int n) {
+  pb::pdl_begin();
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const pb::SamplerRow r = sampled[i];
@@ -878,17 +881,17 @@ uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
                          reinterpret_cast<const uint32_t*>(e->d_positions), nullptr, e->d_states,
                          e->d_sampled, e->stream);
       self->prof_mark(PB_KC_SAMPLER);
-      record_sampler_status<<<blocks, threads, 0, e->stream>>>(
-          e->d_sampled, e->d_samp_status + (size_t)t * n, (int)n);
-      advance_kernel<<<blocks, threads, 0, e->stream>>>(
-          e->d_sampled, e->d_tokens, e->d_positions, e->d_token_log + (size_t)t * n, (int)n);
+      pb::launch_pdl(record_sampler_status, blocks, threads, 0, e->stream, e->d_sampled,
+                     e->d_samp_status + (size_t)t * n, (int)n);
+      pb::launch_pdl(advance_kernel, blocks, threads, 0, e->stream, e->d_sampled, e->d_tokens,
+                     e->d_positions, e->d_token_log + (size_t)t * n, (int)n);
       e->max_span = 4;
       for (uint32_t i = 0; i < n; ++i)
         e->max_span = std::max(e->max_span,
                                (int)((e->slots[seqs[i]].position + done + t + 4) & ~3u));
       // Only the last step's greedy id is published (InferenceStep::selected).
       e->enqueue_forward(n, true, e->d_err + (size_t)t * n, done + t + 1 == steps);
-      increment_kernel<<<blocks, threads, 0, e->stream>>>(e->d_positions, (int)n);
+      pb::launch_pdl(increment_kernel, blocks, threads, 0, e->stream, e->d_positions, (int)n);
       e->launches += 4;
     }
     PB_CUDA(cudaGetLastError());

@@ -308,6 +308,7 @@ __device__ __forceinline__ void tmem_st_same<8>(uint32_t taddr, uint32_t x) {
 template <bool Q4, class C>
 __global__ void __launch_bounds__(C::kThreads, C::kPerSm)
 qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
+  pdl_begin();
   constexpr int NT = C::NT;
   constexpr int S = C::kStages;
   constexpr int CPW = C::kCpw;
@@ -531,7 +532,7 @@ void launch_tc(const TcGemm& g, const Batch& b, unsigned int* status, cudaStream
   }
   const int tiles = g.rtiles * ((b.rows + C::NT - 1) / C::NT);
   const int grid = std::min(tiles, sms * C::kPerSm);
-  qgemm_tc_kernel<Q4, C><<<grid, C::kThreads, C::kBytes, s>>>(g, b, status);
+  launch_pdl(qgemm_tc_kernel<Q4, C>, grid, C::kThreads, C::kBytes, s, g, b, status);
 }
 
 // Tile image of one matrix: grid (chunks, row tiles), thread = row of the tile.

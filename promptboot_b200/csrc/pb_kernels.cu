@@ -20,6 +20,7 @@ namespace pb {
 // fp32_sse2.rs:897-922: hidden = fl(d * (q - 8)), low nibbles are elements 0-15.
 // The token is also recorded in the slot's history (the sampler's penalty set).
 __global__ void embed_kernel(Batch b, const uint8_t* __restrict__ emb) {
+  pdl_begin();
   int row = blockIdx.x;
   uint32_t token = b.tokens[row];
   const uint8_t* w = emb + (size_t)token * 28 * 18;
@@ -38,7 +39,7 @@ __global__ void embed_kernel(Batch b, const uint8_t* __restrict__ emb) {
 }
 
 void launch_embed(const Batch& b, const uint8_t* embedding, cudaStream_t s) {
-  embed_kernel<<<b.rows, 128, 0, s>>>(b, embedding);
+  launch_pdl(embed_kernel, b.rows, 128, 0, s, b, embedding);
 }
 
 // fp32_sse2.rs:1310-1334 then the quantizer.  The reference sums the 896 f64
@@ -53,6 +54,7 @@ constexpr int kNormThreads = kHidden / 4;  // 224: one float4 per thread
 __global__ void __launch_bounds__(kNormThreads)
 rmsnorm_quant_kernel(Batch b, const float* __restrict__ weight, uint32_t layer_ordinal,
                      uint32_t domain) {
+  pdl_begin();
   __shared__ __align__(16) float sq[kHidden];  // squares, then the normalized row
   __shared__ double part[kNormThreads / 32];
   __shared__ int ext[2][kNormThreads / 32];
@@ -124,10 +126,11 @@ rmsnorm_quant_kernel(Batch b, const float* __restrict__ weight, uint32_t layer_o
 
 void launch_rmsnorm_quant(const Batch& b, const float* weight, uint32_t layer_ordinal,
                           uint32_t domain, cudaStream_t s) {
-  rmsnorm_quant_kernel<<<b.rows, kNormThreads, 0, s>>>(b, weight, layer_ordinal, domain);
+  launch_pdl(rmsnorm_quant_kernel, b.rows, kNormThreads, 0, s, b, weight, layer_ordinal, domain);
 }
 
 __global__ void quant_kernel(Batch b, const float* __restrict__ x, size_t ld, int columns) {
+  pdl_begin();
   int row = blockIdx.x;
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int blk = warp; blk < columns / 32; blk += blockDim.x >> 5) {
@@ -136,7 +139,7 @@ __global__ void quant_kernel(Batch b, const float* __restrict__ x, size_t ld, in
 }
 
 void launch_quant(const Batch& b, const float* x, size_t ld, int columns, cudaStream_t s) {
-  quant_kernel<<<b.rows, 256, 0, s>>>(b, x, ld, columns);
+  launch_pdl(quant_kernel, b.rows, 256, 0, s, b, x, ld, columns);
 }
 
 // fp32_sse2.rs:1751-1770 then the quantizer: product = fl(fl(g / (1 + e)) * u)
@@ -146,6 +149,7 @@ constexpr int kSwigluSplit = 4;
 constexpr int kSwigluPerWarp = (kFfn / 32 / kSwigluSplit + 7) / 8;  // 5
 
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(Batch b, uint32_t layer_ordinal) {
+  pdl_begin();
   const int row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int blk0 = blockIdx.y * (kFfn / 32 / kSwigluSplit), blk_end = blk0 + kFfn / 32 / kSwigluSplit;
@@ -176,7 +180,7 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(Batch b, uint32_t lay
 }
 
 void launch_swiglu_quant(const Batch& b, uint32_t layer_ordinal, cudaStream_t s) {
-  swiglu_quant_kernel<<<dim3(b.rows, kSwigluSplit), 256, 0, s>>>(b, layer_ordinal);
+  launch_pdl(swiglu_quant_kernel, dim3(b.rows, kSwigluSplit), 256, 0, s, b, layer_ordinal);
 }
 
 // ------------------------------------------------ block-scaled matvec (GEMV)
@@ -202,6 +206,7 @@ __device__ __forceinline__ uint32_t ld_u32_2aligned(const uint8_t* p) {
 template <int BPB, int RT>
 __global__ void __launch_bounds__(kGemvThreads)
 qgemv_kernel(const uint8_t* __restrict__ w, int rows, int nb, Batch b, Epilogue ep) {
+  pdl_begin();
   extern __shared__ __align__(16) uint8_t smem[];
   const int tid = threadIdx.x;
   const int r0 = blockIdx.x * RT;
@@ -285,18 +290,18 @@ void launch_qgemv(int wtype, const uint8_t* w, int rows, int columns, const Batc
   if (wtype == W_Q4_0) {
     if (nb > 64) {
       constexpr int RT = 8;
-      qgemv_kernel<18, RT><<<rows / RT, kGemvThreads, qgemv_smem<18, RT>(nb), s>>>(w, rows, nb, b, ep);
+      launch_pdl(qgemv_kernel<18, RT>, rows / RT, kGemvThreads, qgemv_smem<18, RT>(nb), s, w, rows, nb, b, ep);
     } else {
       constexpr int RT = 32;
-      qgemv_kernel<18, RT><<<rows / RT, kGemvThreads, qgemv_smem<18, RT>(nb), s>>>(w, rows, nb, b, ep);
+      launch_pdl(qgemv_kernel<18, RT>, rows / RT, kGemvThreads, qgemv_smem<18, RT>(nb), s, w, rows, nb, b, ep);
     }
   } else {
     if (nb > 64) {
       constexpr int RT = 8;
-      qgemv_kernel<34, RT><<<rows / RT, kGemvThreads, qgemv_smem<34, RT>(nb), s>>>(w, rows, nb, b, ep);
+      launch_pdl(qgemv_kernel<34, RT>, rows / RT, kGemvThreads, qgemv_smem<34, RT>(nb), s, w, rows, nb, b, ep);
     } else {
       constexpr int RT = 32;
-      qgemv_kernel<34, RT><<<rows / RT, kGemvThreads, qgemv_smem<34, RT>(nb), s>>>(w, rows, nb, b, ep);
+      launch_pdl(qgemv_kernel<34, RT>, rows / RT, kGemvThreads, qgemv_smem<34, RT>(nb), s, w, rows, nb, b, ep);
     }
   }
 }
@@ -306,6 +311,7 @@ void launch_qgemv(int wtype, const uint8_t* w, int rows, int columns, const Batc
 // fp32_sse2.rs:1413-1428 on q (14 heads) and k (2 heads), then the KV write of
 // inference.rs:1809-1887 (tiled K, row-major V).  Checks: ROPE q, ROPE k, KV k.
 __global__ void rope_kv_kernel(Batch b, int layer, const float* __restrict__ rope) {
+  pdl_begin();
   int row = blockIdx.x;
   int position = b.positions[row];
   uint32_t ord = (uint32_t)layer + 1;
@@ -341,7 +347,7 @@ __global__ void rope_kv_kernel(Batch b, int layer, const float* __restrict__ rop
 }
 
 void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s) {
-  rope_kv_kernel<<<b.rows, 256, 0, s>>>(b, layer, rope);
+  launch_pdl(rope_kv_kernel, b.rows, 256, 0, s, b, layer, rope);
 }
 
 // --------------------------------------------------------------- attention
@@ -354,6 +360,7 @@ void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s
 // Every order-sensitive f64 sum is sequential as in the reference.
 
 __global__ void attention_kernel(Batch b, int layer) {
+  pdl_begin();
   __shared__ float qs[64];
   __shared__ float red[8];
   __shared__ double total;
@@ -408,7 +415,7 @@ void launch_attention(const Batch& b, int layer, int max_span, bool quantize, cu
     launch_attention_grouped(b, layer, (max_span + 3) & ~3, quantize, s);
     return;
   }
-  attention_kernel<<<b.rows * kQHeads, 256, 0, s>>>(b, layer);
+  launch_pdl(attention_kernel, b.rows * kQHeads, 256, 0, s, b, layer);
   if (quantize) launch_quant(b, b.attn, kHidden, kHidden, s);
 }
 
@@ -419,6 +426,7 @@ void launch_attention(const Batch& b, int layer, int max_span, bool quantize, cu
 __global__ void argmax_kernel(const float* __restrict__ logits, size_t ld, int words,
                               uint32_t* ids, uint32_t* bits_out,
                               unsigned long long* first_nonfinite) {
+  pdl_begin();
   __shared__ float bv[32];
   __shared__ int bi[32];
   const float* x = logits + (size_t)blockIdx.x * ld;
@@ -448,7 +456,7 @@ __global__ void argmax_kernel(const float* __restrict__ logits, size_t ld, int w
 
 void launch_argmax(const float* logits, size_t ld, int rows, int words, uint32_t* ids,
                    uint32_t* bits, unsigned long long* first_nonfinite, cudaStream_t s) {
-  argmax_kernel<<<rows, 1024, 0, s>>>(logits, ld, words, ids, bits, first_nonfinite);
+  launch_pdl(argmax_kernel, rows, 1024, 0, s, logits, ld, words, ids, bits, first_nonfinite);
 }
 
 void init_kernel_attributes() {

@@ -9,6 +9,24 @@
 
 namespace pb {
 
+// Launches `kernel` with programmatic stream serialization (the kernel begins
+// with pdl_begin()), so its launch and prologue overlap the previous kernel.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Per-row buffers of one forward batch; row b of every [B][...] array belongs to
 // engine slot slots[b], which owns KV region slots[b] and writes position
 // positions[b] this step.

@@ -121,6 +121,7 @@ sampler_kernel(float* logits, size_t ld, int words, const uint32_t* __restrict__
                const uint64_t* __restrict__ hist_offset, const uint32_t* __restrict__ hist_len,
                const uint8_t* __restrict__ initial_seen, unsigned long long* states,
                SamplerRow* out) {
+  pdl_begin();
   __shared__ uint32_t penal[(kVocab + 31) / 32];
   __shared__ unsigned long long warp_keys[kSampWarps * 20];
   __shared__ unsigned long long top[20];
@@ -230,7 +231,7 @@ void launch_sampler(float* logits, size_t ld, int rows, int words, const uint32_
                     const uint64_t* hist_offset, const uint32_t* hist_len,
                     const uint8_t* initial_seen, unsigned long long* states, SamplerRow* out,
                     cudaStream_t s) {
-  sampler_kernel<<<rows, kSampThreads, 0, s>>>(logits, ld, words, history, hist_offset,
+  launch_pdl(sampler_kernel, rows, kSampThreads, 0, s, logits, ld, words, history, hist_offset,
                                                hist_len, initial_seen, states, out);
 }
 
