@@ -41,6 +41,13 @@ enum Domain : uint32_t {
 __device__ __forceinline__ void pdl_begin() {
   asm volatile("griddepcontrol.launch_dependents;\n\tgriddepcontrol.wait;" ::: "memory");
 }
+// The two halves of pdl_begin, for kernels that do dependency-free work (a
+// weight prefetch) in between: every thread triggers, and every thread that
+// touches global memory written or read by earlier kernels waits first.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ float fbits(uint32_t b) { return __uint_as_float(b); }
 __device__ __forceinline__ uint32_t bitsf(float f) { return __float_as_uint(f); }

@@ -308,7 +308,11 @@ __device__ __forceinline__ void tmem_st_same<8>(uint32_t taddr, uint32_t x) {
 template <bool Q4, class C>
 __global__ void __launch_bounds__(C::kThreads, C::kPerSm)
 qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
-  pdl_begin();
+  // Programmatic dependent launch: the loader prefetches the first stages' weight
+  // tiles (written once at model open) before waiting for the previous kernel;
+  // the epilogue warps wait before touching activations and outputs; the MMA
+  // warp touches no global memory.
+  pdl_trigger();
   constexpr int NT = C::NT;
   constexpr int S = C::kStages;
   constexpr int CPW = C::kCpw;
@@ -365,24 +369,37 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
     if (lane == 0) {
       int q = 0, load_last = -1;
       bool stop = false;
+      // Weight tiles of the first stages of this CTA's first tile.
+      const int pre = blockIdx.x < ntiles ? min(S, nchunks) : 0;
+      if (pre > 0) {
+        const uint8_t* wt0 = g.tiles + (size_t)(blockIdx.x / nst) * nchunks * kTcChunkBytes;
+        for (int c = 0; c < pre; ++c) {
+          mbar_expect_tx(&full[c], C::kStage);
+          bulk_g2s(smem + c * C::kStage, wt0 + (size_t)c * kTcChunkBytes, kTcChunkBytes, &full[c]);
+        }
+      }
+      pdl_wait();
       for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
         const int rt = tile / nst, seq0 = (tile % nst) * NT;
         const uint8_t* wt = g.tiles + (size_t)rt * nchunks * kTcChunkBytes;
         for (int c = 0; c < nchunks; ++c, ++q) {
           const int st = q % S;
-          if (!wait_phase(&empty[st], ((q / S) & 1) ^ 1, abort_flag)) {
-            stop = true;
-            break;
-          }
           uint8_t* sp = smem + st * C::kStage;
-          mbar_expect_tx(&full[st], C::kStage);
-          bulk_g2s(sp, wt + (size_t)c * kTcChunkBytes, kTcChunkBytes, &full[st]);
+          if (q >= pre) {
+            if (!wait_phase(&empty[st], ((q / S) & 1) ^ 1, abort_flag)) {
+              stop = true;
+              break;
+            }
+            mbar_expect_tx(&full[st], C::kStage);
+            bulk_g2s(sp, wt + (size_t)c * kTcChunkBytes, kTcChunkBytes, &full[st]);
+          }
           bulk_g2s(sp + C::kBOff,
                    b.aq_tc + ((size_t)c * (b.tc_seqs >> 3) + (seq0 >> 3)) * kTcGroupBytes,
                    (NT / 8) * kTcGroupBytes, &full[st]);
           load_last = q;
         }
       }
+      if (pre > load_last + 1) load_last = pre - 1;  // prefetched stages still land
       // Every issued copy lands before the CTA may exit.
       for (int k = max(0, load_last - S + 1); k <= load_last; ++k)
         wait_drain(&full[k % S], (k / S) & 1, 50000000ull);
@@ -413,6 +430,7 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
     }
     __syncwarp();
   } else {
+    pdl_wait();
     const int lrow = quarter * 32 + lane;
     const uint64_t neg_magic2 = pk(-12582912.0f, -12582912.0f);
     const float nz = __uint_as_float(g.neg_zero_bits);
