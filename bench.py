@@ -51,7 +51,58 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=8)
     p.add_argument("--cpu-tokens", type=int, default=6, help="CPU-baseline tokens per thread")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--op", choices=["attention", "qmatvec"], default=None,
+                   help="time one operator on synthetic inputs (the small cases of the ncu "
+                        "captures under profiles/) instead of the decode bench")
+    p.add_argument("--op-rows", type=int, default=192, help="--op: sequences")
+    p.add_argument("--op-positions", type=int, default=520, help="--op attention: context")
+    p.add_argument("--op-shape", default="151936x896", help="--op qmatvec: ROWSxCOLS")
+    p.add_argument("--op-wtype", type=int, default=3, help="--op qmatvec: 2 Q4_0, 3 Q8_0")
     return p.parse_args()
+
+
+def run_op(args):
+    """One operator through the C ABI on seeded synthetic device inputs: 3
+    untimed calls, then the mean of 10 timed with CUDA events.  The qmatvec
+    operator includes its per-call tile-image build and activation quantization."""
+    import ctypes
+    import torch
+    from promptboot_b200 import _lib
+    lib = _lib.load()
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    g = torch.Generator(device="cuda").manual_seed(7)
+    rows = args.op_rows
+    if args.op == "attention":
+        cap = (args.op_positions + 11) // 4 * 4
+        kv = torch.randn(rows * 24 * 4 * cap * 64, device="cuda", generator=g) * 0.5
+        q = torch.randn(rows, 896, device="cuda", generator=g)
+        out = torch.empty(rows, 896, device="cuda")
+        pos = (ctypes.c_uint32 * rows)(*([args.op_positions - 1] * rows))
+        call = lambda: lib.pb_attention_device(P(q), P(kv), cap, 0, pos, rows, 0, P(out), None, None)
+        desc = {"rows": rows, "positions": args.op_positions}
+    else:
+        m, k = (int(v) for v in args.op_shape.split("x"))
+        bpb = 18 if args.op_wtype == 2 else 34
+        nb = m * k // 32
+        rng = np.random.default_rng(7)
+        w = rng.integers(0, 256, (nb, bpb), dtype=np.uint8)
+        w[:, :2] = (np.abs(rng.standard_normal(nb) * 0.02) / 8).astype(np.float16).view(np.uint8).reshape(nb, 2)
+        w = torch.from_numpy(w.reshape(-1)).cuda()
+        x = torch.randn(rows, k, device="cuda", generator=g)
+        y = torch.empty(rows, m, device="cuda")
+        call = lambda: lib.pb_qmatvec_device(args.op_wtype, P(w), m, k, P(x), rows, P(y), None)
+        desc = {"rows": rows, "shape": args.op_shape, "wtype": args.op_wtype}
+    for _ in range(3):
+        if call() != 0:
+            raise RuntimeError(f"{args.op} failed: {lib.pb_last_error_string()}")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"op": args.op, **desc, "ms_per_call": e0.elapsed_time(e1) / 10}), flush=True)
 
 
 def dist_setup(args):
@@ -155,15 +206,25 @@ def measured_peaks():
     return 6650.0, 1400.0, "fallback"
 
 
-def profiled_traffic(kernel_class: str):
-    """DRAM bytes per launch from the committed ncu summary, if one covers the class."""
+def profiled_traffic(kernel_class: str, seqs: int, mean_ctx: float):
+    """DRAM bytes per launch at this workload, scaled from the committed ncu
+    capture of a smaller case (profiles/traffic.json), if one covers the class."""
     p = ROOT / "profiles" / "traffic.json"
     if p.exists():
         d = json.loads(p.read_text())
-        if kernel_class in d:
-            return d[kernel_class]
+        if kernel_class == "attention" and "attention" in d:
+            return seqs * mean_ctx * d["attention"]["dram_bytes_per_sequence_position"]
     return None
 
+
+# What bounds each kernel class in practice (ncu captures under profiles/).
+LIMITERS = {
+    "attention": "f32->f64 widening of every product on the XU pipe (57% busy in "
+                 "profiles/attention_kv_group_r192_p520.md); HBM traffic is 1031 B per "
+                 "sequence-position, the algorithmic 1024 B",
+    "gemv": "per-block binary32 epilogue on the FMA pipe and bulk-copy issue "
+            "(profiles/qgemm_tc_*.md)",
+}
 
 KC = {"embed": 0, "norm": 1, "gemv": 2, "rope_kv": 3, "attention": 4, "quant": 5, "swiglu": 6,
       "lm_head": 7, "argmax": 8, "sampler": 9}
@@ -303,7 +364,9 @@ def run_ours(args, world, rank, local):
     hbm, tflops_sus, peak_kind = measured_peaks()
     alg = algorithmic_bytes(dominant, S, start_pos, args.steps)
     achieved = (alg / (dom_ms / 1000.0)) / 1e9 if dom_ms > 0 else None
-    traffic = profiled_traffic(dominant)
+    mean_ctx = start_pos + (args.steps - 1) / 2.0 + 1.0
+    traffic = profiled_traffic(dominant, S, mean_ctx)
+    alg_per_launch = alg / max(dom_n, 1)
 
     line = None
     if rank == 0:
@@ -330,7 +393,9 @@ def run_ours(args, world, rank, local):
             "gpu_launches": int(launches),
             "roofline": {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": (achieved / hbm) if achieved else None,
-                         "traffic": traffic, "peak_source": peak_kind,
+                         "traffic": traffic, "algorithmic_bytes_per_launch": alg_per_launch,
+                         "peak_source": peak_kind,
+                         "limiter": LIMITERS.get(dominant),
                          "launches": int(dom_n), "avg_launch_us": 1000.0 * dom_ms / max(dom_n, 1),
                          "warmup_ms_by_class": {k: round(v, 3) for k, v in by_class.items()}},
             "clocks": clock.summary(),
@@ -344,6 +409,9 @@ def run_ours(args, world, rank, local):
 
 def main():
     args = parse()
+    if args.op:
+        run_op(args)
+        return
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":

@@ -257,7 +257,6 @@ struct TcCfg {
   static_assert((kCols & (kCols - 1)) == 0 && kCols >= 32, "TMEM allocation size");
   static_assert(kPerSm * (kBytes + 1024) <= 233472, "shared memory per SM");
 };
-using CfgLatency = TcCfg<16, 4, 1, 6, 8>;   // 16 epilogue warps, one CTA per SM
 using Cfg16 = TcCfg<16, 8, 2, 4, 4>;
 using Cfg32 = TcCfg<32, 16, 2, 4, 2>;
 using Cfg64 = TcCfg<64, 16, 1, 6, 2>;
@@ -605,50 +604,33 @@ int sm_count() {
 }
 }  // namespace
 
-// Configuration choice: 0 CfgLatency, 1 Cfg16, 2 Cfg32, 3 Cfg64.  With no
-// more tiles than SMs the latency configuration (most epilogue warps per tile)
-// wins; otherwise the one with the smallest busiest-CTA tile count times
-// per-tile epilogue work per SM slot.  PB_TC_TILE=L|16|32|64 in the environment
-// forces one (tests cover every configuration; tuning sweeps).
+// Configuration choice (1 Cfg16, 2 Cfg32, 3 Cfg64), from measurements at 256
+// sequences: wide tiles re-read each weight tile fewer times, which pays once
+// there are several tiles per SM slot (the output head); narrow tiles spread
+// matrices with few row tiles over more SMs.  PB_TC_TILE=16|32|64 in the
+// environment forces one (tests cover every configuration; tuning sweeps).
 int tc_pick_config(int rtiles, int batch) {
   if (const char* f = std::getenv("PB_TC_TILE")) {
-    if (f[0] == 'L') return 0;
     const int nt = std::atoi(f);
     if (nt == 16) return 1;
     if (nt == 32) return 2;
     if (nt == 64) return 3;
   }
-  const int sms = sm_count();
-  if ((long)rtiles * ((batch + 15) / 16) <= sms) return 0;
-  const int nts[3] = {64, 32, 16};
-  const int per_sm[3] = {Cfg64::kPerSm, Cfg32::kPerSm, Cfg16::kPerSm};
-  const int ids[3] = {3, 2, 1};
-  int best = 1;
-  double best_cost = 1e30;
-  for (int i = 0; i < 3; ++i) {
-    const long tiles = (long)rtiles * ((batch + nts[i] - 1) / nts[i]);
-    const long slots = (long)sms * per_sm[i];
-    const long busiest = (tiles + slots - 1) / slots;
-    const double cost = (double)busiest * nts[i] / per_sm[i];
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = ids[i];
-    }
-  }
-  return best;
+  const long sms = sm_count();
+  if ((long)rtiles * ((batch + 63) / 64) >= 4 * sms) return 3;
+  if ((long)rtiles * ((batch + 31) / 32) >= Cfg32::kPerSm * sms) return 2;
+  return 1;
 }
 
 void launch_tc_gemm(const TcGemm& g, const Batch& b, unsigned int* status, cudaStream_t s) {
   const int cfg = tc_pick_config(g.rtiles, b.rows);
   const int sms = sm_count();
   if (g.wtype == W_Q4_0) {
-    if (cfg == 0) launch_tc<true, CfgLatency>(g, b, status, s, sms);
-    else if (cfg == 1) launch_tc<true, Cfg16>(g, b, status, s, sms);
+    if (cfg == 1) launch_tc<true, Cfg16>(g, b, status, s, sms);
     else if (cfg == 2) launch_tc<true, Cfg32>(g, b, status, s, sms);
     else launch_tc<true, Cfg64>(g, b, status, s, sms);
   } else {
-    if (cfg == 0) launch_tc<false, CfgLatency>(g, b, status, s, sms);
-    else if (cfg == 1) launch_tc<false, Cfg16>(g, b, status, s, sms);
+    if (cfg == 1) launch_tc<false, Cfg16>(g, b, status, s, sms);
     else if (cfg == 2) launch_tc<false, Cfg32>(g, b, status, s, sms);
     else launch_tc<false, Cfg64>(g, b, status, s, sms);
   }
