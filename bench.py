@@ -36,7 +36,6 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decoded tok/s, Qwen2.5-0.5B Q4_0 batch 256 at 1/2/4/8 B200; % HBM roofline"
 UNIT = "tok/s"
-PROMPT_SEED = 0x5EED0000
 
 
 def parse():
@@ -119,20 +118,7 @@ def dist_setup(args):
     return world, rank, local
 
 
-def barrier(world):
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-
-
-def max_over_ranks(value: float, world: int) -> float:
-    if world == 1:
-        return value
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+from promptboot_b200.shard import barrier, max_over_ranks, aggregate_throughput  # noqa: E402
 
 
 def model_image(rank: int, world: int):
@@ -287,7 +273,7 @@ def run_reference(args, world, rank):
 def run_ours(args, world, rank, local):
     import ctypes
     import torch
-    from promptboot_b200 import _lib, api
+    from promptboot_b200 import _lib, api, shard
     torch.cuda.set_device(local)
     img = model_image(rank, world)
     S, P, C = args.seqs, args.prompt, args.context
@@ -297,13 +283,12 @@ def run_ours(args, world, rank, local):
     eng = api.InferenceEngine(model, max_seqs=S, max_context=C)
     lib = _lib.load()
     seqs = np.arange(S, dtype=np.uint32)
-    gidx = rank * S + np.arange(S)
-    prompts = np.stack([np.random.default_rng(PROMPT_SEED + int(g)).integers(0, 151643, P, dtype=np.uint32)
-                        for g in gidx])
+    gidx = shard.global_sequences(rank, world, S)
+    prompts = shard.prompts_for(rank, world, S, P)
     status, _, errs = eng.prefill_batch(seqs, prompts, C - P)
     if status:
         raise RuntimeError(f"prefill failed: {errs[0].tuple()}")
-    states = [api.SamplingState(int(g)) for g in gidx]
+    states = [api.SamplingState(shard.sampling_seed(g)) for g in gidx]
     stream = torch.cuda.ExternalStream(lib.pb_engine_stream(eng._h))
 
     # warm-up with every kernel class timed, to name the dominant kernel
@@ -358,9 +343,8 @@ def run_ours(args, world, rank, local):
     barrier(world)
     e2e_ms = max_over_ranks(a0.elapsed_time(a1), world)
 
-    total_tokens = S * world * args.steps
-    value = total_tokens / (elapsed_ms / 1000.0)
-    e2e_value = S * world * e2e_steps / (e2e_ms / 1000.0)
+    value = aggregate_throughput(S * args.steps, world, elapsed_ms)
+    e2e_value = aggregate_throughput(S * e2e_steps, world, e2e_ms)
     hbm, tflops_sus, peak_kind = measured_peaks()
     alg = algorithmic_bytes(dominant, S, start_pos, args.steps)
     achieved = (alg / (dom_ms / 1000.0)) / 1e9 if dom_ms > 0 else None
