@@ -16,8 +16,8 @@
 // words: lane (tile, pair) reads positions 4 tile + 2 pair + {0, 1} of one
 // component with one 8-byte load, and a half-warp covers all 32 banks once.
 // V chunks (row-major, 64 positions) reuse the two buffers.  Every lane keeps
-// two independent f64 chains (two positions in QK, components c and c + 32 in
-// PV).  Scores live in shared memory, so this path serves contexts up to
+// two independent f64 chains (two positions in QK, components 2 lane and
+// 2 lane + 1 in PV, one 8-byte load per position).  Scores live in shared memory, so this path serves contexts up to
 // kAttnMaxPositions; longer ones use the per-head kernel.
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
@@ -153,12 +153,13 @@ attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize) {
     for (int p = lane; p < span; p += 32) dst[p] = score[p];
   }
 
-  // ---- values: lane owns components lane and lane + 32 of head h, positions in order
+  // ---- values: lane owns components 2 lane and 2 lane + 1 of head h (one
+  // 8-byte load per position), positions in order
   double acc0 = 0.0, acc1 = 0.0;
   for (int t = 0; t < nchunks; ++t) {
     cp_wait1();
     __syncthreads();
-    const float* vt = bufs[t & 1];
+    const float* vt = bufs[t & 1] + 2 * lane;
     const float* pr = score + t * kChunk;
     const int rows_here = min(kChunk, positions - t * kChunk);
     int i = 0;
@@ -167,13 +168,15 @@ attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize) {
       const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        acc0 += (double)__fmul_rn(pv[j], vt[(i + j) * 64 + lane]);
-        acc1 += (double)__fmul_rn(pv[j], vt[(i + j) * 64 + lane + 32]);
+        const float2 v2 = *reinterpret_cast<const float2*>(vt + (i + j) * 64);
+        acc0 += (double)__fmul_rn(pv[j], v2.x);
+        acc1 += (double)__fmul_rn(pv[j], v2.y);
       }
     }
     for (; i < rows_here; ++i) {
-      acc0 += (double)__fmul_rn(pr[i], vt[i * 64 + lane]);
-      acc1 += (double)__fmul_rn(pr[i], vt[i * 64 + lane + 32]);
+      const float2 v2 = *reinterpret_cast<const float2*>(vt + i * 64);
+      acc0 += (double)__fmul_rn(pr[i], v2.x);
+      acc1 += (double)__fmul_rn(pr[i], v2.y);
     }
     __syncthreads();
     if (t + 2 < nchunks) load_v(t + 2, bufs[t & 1]);
@@ -183,15 +186,20 @@ attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize) {
   const float o0 = (float)acc0, o1 = (float)acc1;
   const int qh_index = kh * kHeadsPerKv + h;
   float* out = b.attn + (size_t)row * kHidden + qh_index * 64;
-  out[lane] = o0;
-  out[lane + 32] = o1;
-  check_finite(o0, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + lane);
-  check_finite(o1, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + lane + 32);
+  *reinterpret_cast<float2*>(out + 2 * lane) = make_float2(o0, o1);
+  // Stage checks in index order within the lane (the row's atomicMin keeps the
+  // lowest index anyway).
+  check_finite(o0, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + 2 * lane);
+  check_finite(o1, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + 2 * lane + 1);
   if (quantize) {
     // Head qh's 64 outputs are Q8_0 blocks 2 qh and 2 qh + 1 of the
-    // o-projection input, one value per lane each.
-    quantize_row_block(b, o0, row, 2 * qh_index);
-    quantize_row_block(b, o1, row, 2 * qh_index + 1);
+    // o-projection input; element e of a block sits in lane e / 2 (+ 16 for the
+    // second block), slot e % 2.
+    const int src0 = lane >> 1, src1 = 16 + (lane >> 1);
+    const float a0 = __shfl_sync(0xffffffffu, o0, src0), a1 = __shfl_sync(0xffffffffu, o1, src0);
+    const float b0 = __shfl_sync(0xffffffffu, o0, src1), b1 = __shfl_sync(0xffffffffu, o1, src1);
+    quantize_row_block(b, (lane & 1) ? a1 : a0, row, 2 * qh_index);
+    quantize_row_block(b, (lane & 1) ? b1 : b0, row, 2 * qh_index + 1);
   }
 }
 

@@ -227,16 +227,18 @@ constexpr int kDwOff = kKC * kATile;
 constexpr uint32_t kMagic = 0x4B400000u;  // binary32 1.5 * 2^23
 static_assert(kDwOff + kM * kKC * 4 == kTcChunkBytes, "tile image chunk size");
 
-// Kernel configurations: NT sequences per tile, CPW TMEM columns per epilogue
-// warp (4 lane quarters x NT / CPW column groups), PER_SM resident CTAs per SM
+// Kernel configurations: NT = MMA N, SEQ <= NT sequences per tile (a half-filled
+// N=16 MMA doubles the tiles of matrices with few row tiles), CPW TMEM columns
+// per epilogue warp (4 lane quarters x SEQ / CPW column groups), PER_SM resident CTAs per SM
 // (shared memory, TMEM columns and registers sized for that count), STAGES ring
 // depth.  Wide tiles for many tiles per SM, narrow tiles with many epilogue
 // warps when there are about as many tiles as SMs (latency-bound).
-template <int NT_, int CPW_, int PER_SM_, int STAGES_, int GROUPS_>
+template <int NT_, int CPW_, int PER_SM_, int STAGES_, int GROUPS_, int SEQ_ = NT_>
 struct TcCfg {
-  static constexpr int NT = NT_;
+  static constexpr int NT = NT_;    // MMA N (TMEM columns per block)
+  static constexpr int SEQ = SEQ_;  // sequences per tile (<= NT; rows SEQ..NT-1 of B unused)
   static constexpr int kCpw = CPW_;
-  static constexpr int kEpiWarps = 4 * NT / kCpw;
+  static constexpr int kEpiWarps = 4 * SEQ / kCpw;
   static constexpr int kThreads = (2 + kEpiWarps) * 32;
   static constexpr int kPerSm = PER_SM_;
   static constexpr int kStages = STAGES_;
@@ -247,16 +249,19 @@ struct TcCfg {
   static constexpr int kBatch = kCpw * kKC <= 16 ? kKC : 2;
   static constexpr int kBOff = kTcChunkBytes;  // [NT/8] groups of kTcGroupBytes
   static constexpr int kStage = kBOff + (NT / 8) * kTcGroupBytes;
+  static constexpr uint32_t kTxBytes = kTcChunkBytes + (SEQ / 8) * kTcGroupBytes;  // per chunk
   static constexpr int kBarOff = kStages * kStage;
   static constexpr int kBytes = kBarOff + (2 * kStages + 2 * kGroups) * 8 + 16;
   static constexpr uint32_t kCols = kGroups * kKC * NT;
   static_assert(kStage % 128 == 0, "stage alignment");
   static_assert(kCpw == 4 || kCpw == 8 || kCpw == 16, "epilogue column batch");
   static_assert(kThreads <= 1024, "block size");
+  static_assert(SEQ % 8 == 0 && SEQ <= NT && SEQ % kCpw == 0, "sequence tile");
   static_assert(kPerSm * kCols <= 512, "TMEM columns per SM");
   static_assert((kCols & (kCols - 1)) == 0 && kCols >= 32, "TMEM allocation size");
   static_assert(kPerSm * (kBytes + 1024) <= 233472, "shared memory per SM");
 };
+using Cfg8 = TcCfg<16, 8, 3, 3, 2, 8>;
 using Cfg16 = TcCfg<16, 8, 2, 4, 4>;
 using Cfg32 = TcCfg<32, 16, 2, 4, 2>;
 using Cfg64 = TcCfg<64, 16, 1, 6, 2>;
@@ -313,6 +318,7 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
   // warp touches no global memory.
   pdl_trigger();
   constexpr int NT = C::NT;
+  constexpr int SEQ = C::SEQ;
   constexpr int S = C::kStages;
   constexpr int CPW = C::kCpw;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -331,7 +337,7 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nchunks = g.nb / kKC;
-  const int nst = (b.rows + NT - 1) / NT;  // sequence tiles
+  const int nst = (b.rows + SEQ - 1) / SEQ;  // sequence tiles
   const int ntiles = g.rtiles * nst;
   const int quarter = warp & 3, cg = (warp - 2) >> 2;  // epilogue warps only
 
@@ -373,13 +379,13 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
       if (pre > 0) {
         const uint8_t* wt0 = g.tiles + (size_t)(blockIdx.x / nst) * nchunks * kTcChunkBytes;
         for (int c = 0; c < pre; ++c) {
-          mbar_expect_tx(&full[c], C::kStage);
+          mbar_expect_tx(&full[c], C::kTxBytes);
           bulk_g2s(smem + c * C::kStage, wt0 + (size_t)c * kTcChunkBytes, kTcChunkBytes, &full[c]);
         }
       }
       pdl_wait();
       for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
-        const int rt = tile / nst, seq0 = (tile % nst) * NT;
+        const int rt = tile / nst, seq0 = (tile % nst) * SEQ;
         const uint8_t* wt = g.tiles + (size_t)rt * nchunks * kTcChunkBytes;
         for (int c = 0; c < nchunks; ++c, ++q) {
           const int st = q % S;
@@ -389,12 +395,12 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
               stop = true;
               break;
             }
-            mbar_expect_tx(&full[st], C::kStage);
+            mbar_expect_tx(&full[st], C::kTxBytes);
             bulk_g2s(sp, wt + (size_t)c * kTcChunkBytes, kTcChunkBytes, &full[st]);
           }
           bulk_g2s(sp + C::kBOff,
                    b.aq_tc + ((size_t)c * (b.tc_seqs >> 3) + (seq0 >> 3)) * kTcGroupBytes,
-                   (NT / 8) * kTcGroupBytes, &full[st]);
+                   (SEQ / 8) * kTcGroupBytes, &full[st]);
           load_last = q;
         }
       }
@@ -501,8 +507,8 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
       }
       if (stop) break;
       // Tile done: epilogue stores for rows of this warp's lane quarter.
-      const int rt = tile / nst, seq0 = (tile % nst) * NT;
-      const int nseq = min(NT, b.rows - seq0);
+      const int rt = tile / nst, seq0 = (tile % nst) * SEQ;
+      const int nseq = min(SEQ, b.rows - seq0);
       int si = 0;
       while (si + 1 < g.nseg && rt >= g.seg[si].rtile_end) ++si;
       const Epilogue& ep = g.seg[si].ep;
@@ -547,7 +553,7 @@ void launch_tc(const TcGemm& g, const Batch& b, unsigned int* status, cudaStream
     cudaFuncSetAttribute(qgemm_tc_kernel<Q4, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kBytes);
     configured = true;
   }
-  const int tiles = g.rtiles * ((b.rows + C::NT - 1) / C::NT);
+  const int tiles = g.rtiles * ((b.rows + C::SEQ - 1) / C::SEQ);
   const int grid = std::min(tiles, sms * C::kPerSm);
   launch_pdl(qgemm_tc_kernel<Q4, C>, grid, C::kThreads, C::kBytes, s, g, b, status);
 }
@@ -604,19 +610,22 @@ int sm_count() {
 }
 }  // namespace
 
-// Configuration choice (1 Cfg16, 2 Cfg32, 3 Cfg64), from measurements at 256
-// sequences: wide tiles re-read each weight tile fewer times, which pays once
-// there are several tiles per SM slot (the output head); narrow tiles spread
-// matrices with few row tiles over more SMs.  PB_TC_TILE=16|32|64 in the
-// environment forces one (tests cover every configuration; tuning sweeps).
+// Configuration choice (0 Cfg8, 1 Cfg16, 2 Cfg32, 3 Cfg64), from measurements
+// at 256 sequences: wide tiles re-read each weight tile fewer times, which pays
+// once there are several tiles per SM slot (the output head); narrow tiles
+// spread matrices with few row tiles (q/k/v, o, down) over more SMs.
+// PB_TC_TILE=8|16|32|64 in the environment forces one (tests cover every
+// configuration; tuning sweeps).
 int tc_pick_config(int rtiles, int batch) {
   if (const char* f = std::getenv("PB_TC_TILE")) {
     const int nt = std::atoi(f);
+    if (nt == 8) return 0;
     if (nt == 16) return 1;
     if (nt == 32) return 2;
     if (nt == 64) return 3;
   }
   const long sms = sm_count();
+  if ((long)rtiles * ((batch + 15) / 16) <= sms) return 0;
   if ((long)rtiles * ((batch + 63) / 64) >= 4 * sms) return 3;
   if ((long)rtiles * ((batch + 31) / 32) >= Cfg32::kPerSm * sms) return 2;
   return 1;
@@ -626,11 +635,13 @@ void launch_tc_gemm(const TcGemm& g, const Batch& b, unsigned int* status, cudaS
   const int cfg = tc_pick_config(g.rtiles, b.rows);
   const int sms = sm_count();
   if (g.wtype == W_Q4_0) {
-    if (cfg == 1) launch_tc<true, Cfg16>(g, b, status, s, sms);
+    if (cfg == 0) launch_tc<true, Cfg8>(g, b, status, s, sms);
+    else if (cfg == 1) launch_tc<true, Cfg16>(g, b, status, s, sms);
     else if (cfg == 2) launch_tc<true, Cfg32>(g, b, status, s, sms);
     else launch_tc<true, Cfg64>(g, b, status, s, sms);
   } else {
-    if (cfg == 1) launch_tc<false, Cfg16>(g, b, status, s, sms);
+    if (cfg == 0) launch_tc<false, Cfg8>(g, b, status, s, sms);
+    else if (cfg == 1) launch_tc<false, Cfg16>(g, b, status, s, sms);
     else if (cfg == 2) launch_tc<false, Cfg32>(g, b, status, s, sms);
     else launch_tc<false, Cfg64>(g, b, status, s, sms);
   }

@@ -241,7 +241,7 @@ def test_matvec_shapes_match_oracle(wtype, rows, cols, batch):
         assert np.array_equal(u32(got[b]), u32(ref)), b
 
 
-@pytest.mark.parametrize("tile", ["16", "32", "64"])
+@pytest.mark.parametrize("tile", ["8", "16", "32", "64"])
 @pytest.mark.parametrize("wtype,rows,cols,batch", [(2, 896, 4864, 100), (3, 1024, 896, 130),
                                                    (2, 1152, 896, 64)])
 def test_tensor_core_every_tile_width(monkeypatch, tile, wtype, rows, cols, batch):
