@@ -41,6 +41,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <type_traits>
 
 namespace pb {
 namespace {
@@ -471,31 +472,43 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
 #pragma unroll
           for (int jj = 0; jj < BT; ++jj) tmem_st_same<CPW>(tg + (uint32_t)((jb + jj) * NT), kMagic);
           uint64_t w2[BT], n2[BT];
+          bool exact_fma = true;  // Q4_0: fma(x, dW, -1.5*2^23*dW) needs a finite dW
 #pragma unroll
           for (int jj = 0; jj < BT; ++jj) {
             w2[jj] = pk(dw[jb + jj], dw[jb + jj]);
             const float nm = -__fmul_rn(12582912.0f, dw[jb + jj]);
             n2[jj] = pk(nm, nm);
+            exact_fma = exact_fma && finite_bits(__float_as_uint(dw[jb + jj]));
           }
+          exact_fma = __all_sync(0xffffffffu, exact_fma);
+          // Warp-uniform choice of the Q4_0 product form (two unrolled copies).
+          auto accumulate = [&](auto fast) {
 #pragma unroll
-          for (int p = 0; p < CPW / 2; ++p) {
-            uint64_t a = acc[p];
+            for (int p = 0; p < CPW / 2; ++p) {
+              uint64_t a = acc[p];
 #pragma unroll
-            for (int jj = 0; jj < BT; ++jj) {
-              const int s = s0 + 2 * p;
-              const uint64_t da2 = *reinterpret_cast<const uint64_t*>(
-                  sp + C::kBOff + (s >> 3) * kTcGroupBytes + 1024 + ((jb + jj) * 8 + (s & 7)) * 4);
-              const uint64_t x2 = pk_u(v[jj][2 * p], v[jj][2 * p + 1]);
-              uint64_t t;
-              if (Q4) {
-                t = fma2(fma2(x2, w2[jj], n2[jj]), da2, z2);
-              } else {
-                t = fma2(add2(x2, neg_magic2), mul2(w2[jj], da2), z2);
+              for (int jj = 0; jj < BT; ++jj) {
+                const int s = s0 + 2 * p;
+                const uint64_t da2 = *reinterpret_cast<const uint64_t*>(
+                    sp + C::kBOff + (s >> 3) * kTcGroupBytes + 1024 + ((jb + jj) * 8 + (s & 7)) * 4);
+                const uint64_t x2 = pk_u(v[jj][2 * p], v[jj][2 * p + 1]);
+                uint64_t t;
+                if (Q4) {
+                  // Non-finite dW (never in a sane image): fl(f32(i) * dW) with
+                  // f32(i) = x - 1.5*2^23 exactly, as the reference computes it.
+                  const uint64_t idw = decltype(fast)::value ? fma2(x2, w2[jj], n2[jj])
+                                                             : fma2(add2(x2, neg_magic2), w2[jj], z2);
+                  t = fma2(idw, da2, z2);
+                } else {
+                  t = fma2(add2(x2, neg_magic2), mul2(w2[jj], da2), z2);
+                }
+                a = add2(a, t);
               }
-              a = add2(a, t);
+              acc[p] = a;
             }
-            acc[p] = a;
-          }
+          };
+          if (!Q4 || exact_fma) accumulate(std::true_type{});
+          else accumulate(std::false_type{});
         }
         tmem_wait_st();
         tc_before_sync();

@@ -221,3 +221,37 @@ def test_nonfinite_weight_faults_with_reference_error(model_image):
     assert x.value.tuple()[:2] == [1, 2] and x.value.detail == (1 << 32) | 3
     e.close()
     view.close()
+
+
+def test_tensor_core_up_stage_fault_matches_cuda_core_path(model_image):
+    """An infinite binary16 scale in one block of layer 1's up matrix (row 100)
+    makes the UP stage fail at element 100.  The tensor-core path (12 sequences;
+    its Q4_0 epilogue falls back from the fma form for a non-finite scale)
+    reports the same error tuple, value bits included, as the CUDA-core path
+    (1 sequence)."""
+    img = model_image.copy()
+    tid = pbtqw25.layer_tensor(1, 13)
+    off = int(np.frombuffer(img[pbtqw25.TENSOR_DIR + tid * 96 + 32:][:8].tobytes(), np.uint64)[0])
+    blk = off + (100 * 28 + 3) * 18
+    img[blk:blk + 2] = np.frombuffer(np.uint16(0x7C00).tobytes(), np.uint8)
+    view = api.ModelView(img)
+    p = prompt(3, seed=5)
+    e1 = api.InferenceEngine(view, max_seqs=1, max_context=64)
+    with pytest.raises(api.InferenceError) as x:
+        e1.prefill(p, 4, np.zeros(api.VOCAB, dtype=np.uint32))
+    t1 = x.value.tuple()
+    assert t1[:6] == [6, 14, 1, 0, tid, 0] and t1[7] == (7 << 32) | 100
+    e1.close()
+    n = 12
+    e12 = api.InferenceEngine(view, max_seqs=n, max_context=64)
+    seqs = np.arange(n, dtype=np.uint32)
+    status, _, errs = e12.prefill_batch(seqs, np.stack([p] * n), 4)
+    assert status != 0
+    for er in errs:
+        t = er.tuple()
+        assert t[:6] == t1[:6] and t[7] == t1[7]
+        assert t[6] & 0x7F800000 == 0x7F800000
+        if t1[6] & 0x7FFFFF == 0:  # an infinity: identical bits on both paths
+            assert t[6] == t1[6]
+    e12.close()
+    view.close()
