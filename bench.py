@@ -50,7 +50,7 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=8)
     p.add_argument("--cpu-tokens", type=int, default=6, help="CPU-baseline tokens per thread")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--op", choices=["attention", "qmatvec"], default=None,
+    p.add_argument("--op", choices=["attention", "qmatvec", "matvec-sweep", "sampler"], default=None,
                    help="time one operator on synthetic inputs (the small cases of the ncu "
                         "captures under profiles/) instead of the decode bench")
     p.add_argument("--op-rows", type=int, default=192, help="--op: sequences")
@@ -58,6 +58,111 @@ def parse():
     p.add_argument("--op-shape", default="151936x896", help="--op qmatvec: ROWSxCOLS")
     p.add_argument("--op-wtype", type=int, default=3, help="--op qmatvec: 2 Q4_0, 3 Q8_0")
     return p.parse_args()
+
+
+def run_matvec_sweep(args):
+    """Config 2 (linear sweep): the engine's matvec on the model's own tensors,
+    896->896 (q), 896->128 (k), 896->4864 (gate), 4864->896 (down) Q4_0 and the
+    896->151936 Q8_0 output head, at B in {1, 8, 64, 256}.  Each timed call is
+    bracketed by CUDA events after a 256 MB write that flushes L2; mean of 10
+    calls after 3 untimed ones.  Algorithmic bytes = W + B*K*4 + B*N*4, flops =
+    2*B*N*K (SURVEY config 2)."""
+    import ctypes
+    import torch
+    from promptboot_b200 import _lib, api, pbtqw25
+    lib = _lib.load()
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    img = pbtqw25.load_or_synthesize(0)
+    view = api.ModelView(img)
+    hbm, _, peak_kind = measured_peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    shapes = [("q 896x896 Q4_0", pbtqw25.layer_tensor(0, 19), 896, 896, 18),
+              ("k 128x896 Q4_0", pbtqw25.layer_tensor(0, 16), 128, 896, 18),
+              ("gate 4864x896 Q4_0", pbtqw25.layer_tensor(0, 12), 4864, 896, 18),
+              ("down 896x4864 Q4_0", pbtqw25.layer_tensor(0, 11), 896, 4864, 18),
+              ("head 151936x896 Q8_0", 290, 151936, 896, 34)]
+    out = []
+    for name, tid, n, k, bpb in shapes:
+        for bsz in (1, 8, 64, 256):
+            x = torch.randn(bsz, k, device="cuda")
+            y = torch.empty(bsz, n, device="cuda")
+            for _ in range(3):
+                assert lib.pb_model_matvec_device(view._h, tid, P(x), bsz, P(y), None) == 0
+            total = 0.0
+            for _ in range(10):
+                flush.fill_(1.0)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                lib.pb_model_matvec_device(view._h, tid, P(x), bsz, P(y), None)
+                e1.record()
+                torch.cuda.synchronize()
+                total += e0.elapsed_time(e1)
+            assert lib.pb_model_matvec_status(view._h, None) == 0
+            us = total / 10 * 1000.0
+            nbytes = n * k // 32 * bpb + bsz * k * 4 + bsz * n * 4
+            gbs = nbytes / (us * 1e-6) / 1e9
+            out.append({"shape": name, "batch": bsz, "us": round(us, 2), "alg_bytes": nbytes,
+                        "GB_s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 3),
+                        "int8_TOPS": round(2.0 * bsz * n * k / (us * 1e-6) / 1e12, 2),
+                        "path": "tensor-core" if bsz >= 9 else "cuda-core"})
+    view.close()
+    print(json.dumps({"op": "matvec-sweep", "config": "config 2 linear sweep", "peak_GB_s": hbm,
+                      "peak_source": peak_kind, "l2": "256 MB write between timed calls",
+                      "cases": out}), flush=True)
+
+
+def run_sampler_batch(args):
+    """Config 1 (sampler batch): 256 rows of 151,936 logits ~ N(0, 3^2) with 5
+    positions per row raised by 12 (numpy default_rng(7)), 512 history ids per
+    row, per-row SamplingState(7 + row).  The sampler mutates the logits (the
+    penalty), so every timed call gets a fresh copy (copy not timed); mean of 10
+    calls after 3 untimed.  Algorithmic bytes per batch = 256 x (151,936 x 4 +
+    512 x 8) (SURVEY config 1)."""
+    import ctypes
+    import torch
+    from promptboot_b200 import _lib
+    lib = _lib.load()
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    rows, vocab, hist = 256, 151936, 512
+    rng = np.random.default_rng(7)
+    logits = (rng.standard_normal((rows, vocab)) * 3.0).astype(np.float32)
+    for r in range(rows):
+        logits[r, rng.integers(0, vocab, 5)] += 12.0
+    history = rng.integers(0, vocab, (rows, hist), dtype=np.int64).astype(np.int32)
+    src = torch.from_numpy(logits).cuda()
+    work = torch.empty_like(src)
+    hist_d = torch.from_numpy(history.reshape(-1)).cuda()
+    offs = torch.arange(rows, dtype=torch.int64, device="cuda") * hist
+    lens = torch.full((rows,), hist, dtype=torch.int32, device="cuda")
+    states0 = np.zeros((rows, 2), dtype=np.uint64)
+    for r in range(rows):
+        st = _lib.PbSamplingState()
+        lib.pb_sampling_state_init(ctypes.byref(st), 7 + r)
+        states0[r] = [st.state, st.draws]
+    states = torch.from_numpy(states0.view(np.int64)).cuda()
+    out = torch.empty((rows, 4), dtype=torch.int32, device="cuda")
+    call = lambda: lib.pb_sample_batch_device(P(work), vocab, rows, P(hist_d), P(offs), P(lens),
+                                              P(states), P(out), None)
+    for _ in range(3):
+        work.copy_(src)
+        assert call() == 0
+    total = 0.0
+    for _ in range(10):
+        work.copy_(src)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        call()
+        e1.record()
+        torch.cuda.synchronize()
+        total += e0.elapsed_time(e1)
+    us = total / 10 * 1000.0
+    nbytes = rows * (vocab * 4 + hist * 8)
+    hbm, _, peak_kind = measured_peaks()
+    print(json.dumps({"op": "sampler", "config": "config 1 sampler batch", "rows": rows,
+                      "us_per_batch": round(us, 2), "alg_bytes": nbytes,
+                      "GB_s": round(nbytes / (us * 1e-6) / 1e9, 1),
+                      "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 3),
+                      "peak_source": peak_kind}), flush=True)
 
 
 def run_op(args):
@@ -393,6 +498,12 @@ def run_ours(args, world, rank, local):
 
 def main():
     args = parse()
+    if args.op == "matvec-sweep":
+        run_matvec_sweep(args)
+        return
+    if args.op == "sampler":
+        run_sampler_batch(args)
+        return
     if args.op:
         run_op(args)
         return

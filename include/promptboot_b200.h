@@ -214,6 +214,18 @@ PB_API uint32_t pb_qmatvec_device(uint32_t wtype, const uint8_t *w_device, uint3
 PB_API uint32_t pb_qmatvec_device_noalloc(uint32_t wtype, const uint8_t *w_device, uint32_t rows,
                                           uint32_t cols, const float *x_device, uint32_t batch,
                                           float *y_device, void *stream);
+/* y[b] = model tensor `tensor_id` (a layer's q/k/v/o/gate/up/down matrix or the
+ * Q8_0 output head, id 290) times the Q8_0-quantized x[b], x f32 [batch][cols]:
+ * the engine's own matvec (the tensor-core path on the model's tile image from
+ * 9 rows, the CUDA-core path below).  Asynchronous on `stream`, no per-call
+ * allocation once the model's scratch has grown to the batch (batch <= 256);
+ * pb_model_matvec_status synchronizes `stream` and reports a pipeline timeout of
+ * any earlier call (PB_DEVICE) once.  Replaces the row loop of
+ * inference_q4_matvec_rows_prepared / inference_q8_matvec_rows_prepared
+ * (fp32_sse2.rs:1217-1281) over ModelView::tensor (model.rs:652). */
+PB_API uint32_t pb_model_matvec_device(pb_model *model, uint32_t tensor_id, const float *x_device,
+                                       uint32_t batch, float *y_device, void *stream);
+PB_API uint32_t pb_model_matvec_status(pb_model *model, void *stream);
 /* Q8_0 staging in the reference's 34-byte block format for [rows][cols] f32. */
 PB_API uint32_t pb_quantize_q8_device(const float *x_device, uint32_t rows, uint32_t cols,
                                uint8_t *staging_device, void *stream);

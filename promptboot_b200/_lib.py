@@ -104,6 +104,8 @@ SIGNATURES = {
     "pb_top_logits_8": (u32, [P, u64, P, E]),
     "pb_sample_batch_device": (u32, [P, u64, u32, P, P, P, P, P, P]),
     "pb_qmatvec_device": (u32, [u32, P, u32, u32, P, u32, P, P]),
+    "pb_model_matvec_device": (u32, [P, u32, P, u32, P, P]),
+    "pb_model_matvec_status": (u32, [P, P]),
     "pb_qmatvec_device_noalloc": (u32, [u32, P, u32, u32, P, u32, P, P]),
     "pb_quantize_q8_device": (u32, [P, u32, u32, P, P]),
     "pb_rmsnorm_device": (u32, [P, P, u32, P, P]),

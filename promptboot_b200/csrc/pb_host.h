@@ -51,6 +51,10 @@ struct pb_model {
   uint8_t* tc = nullptr;
   size_t tc_bytes = 0;
   size_t tc_qkv[24] = {}, tc_o[24] = {}, tc_gateup[24] = {}, tc_down[24] = {}, tc_head = 0;
+  // Scratch of pb_model_matvec_device (grown on demand) and its pipeline status word.
+  uint8_t* op_scratch = nullptr;
+  size_t op_scratch_bytes = 0;
+  unsigned int* op_status = nullptr;
   const uint8_t* tensor(uint32_t id) const {
     return data + (offset[id] - pb::kTensorSection);
   }

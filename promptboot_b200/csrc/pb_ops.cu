@@ -284,6 +284,102 @@ uint32_t pb_qmatvec_device(uint32_t wtype, const uint8_t* w, uint32_t rows, uint
   return PB_OK;
 }
 
+namespace {
+
+// The model tensor behind pb_model_matvec_device: weights, shape and, for the
+// tensor-core path, its tile image inside the model's stacked images.
+struct ModelMatrix {
+  int wtype = 0, rows = 0, cols = 0;
+  const uint8_t* w = nullptr;
+  const uint8_t* image = nullptr;
+};
+
+bool model_matrix(const pb_model* m, uint32_t id, ModelMatrix* out) {
+  if (id == 290) {
+    *out = {pb::W_Q8_0, pb::kVocab, 896, m->tensor(290), m->tc + m->tc_head};
+    return true;
+  }
+  if (id < 1 || id > 288) return false;
+  const int layer = (int)(id - 1) / 12;
+  const uint32_t role = 10 + (id - 1) % 12;
+  const size_t i896 = pb::tc_image_bytes(896, 896), i128 = pb::tc_image_bytes(128, 896);
+  const size_t i4864 = pb::tc_image_bytes(4864, 896);
+  const uint8_t* tc = m->tc;
+  switch (role) {
+    case 19: *out = {pb::W_Q4_0, 896, 896, m->tensor(id), tc + m->tc_qkv[layer]}; return true;
+    case 16: *out = {pb::W_Q4_0, 128, 896, m->tensor(id), tc + m->tc_qkv[layer] + i896}; return true;
+    case 21: *out = {pb::W_Q4_0, 128, 896, m->tensor(id), tc + m->tc_qkv[layer] + i896 + i128}; return true;
+    case 17: *out = {pb::W_Q4_0, 896, 896, m->tensor(id), tc + m->tc_o[layer]}; return true;
+    case 12: *out = {pb::W_Q4_0, 4864, 896, m->tensor(id), tc + m->tc_gateup[layer]}; return true;
+    case 13: *out = {pb::W_Q4_0, 4864, 896, m->tensor(id), tc + m->tc_gateup[layer] + i4864}; return true;
+    case 11: *out = {pb::W_Q4_0, 896, 4864, m->tensor(id), tc + m->tc_down[layer]}; return true;
+    default: return false;
+  }
+}
+
+}  // namespace
+
+uint32_t pb_model_matvec_device(pb_model* m, uint32_t id, const float* x, uint32_t batch, float* y,
+                                void* stream) {
+  ModelMatrix mm;
+  if (!m || !x || !y || batch == 0 || batch > 256 || !model_matrix(m, id, &mm)) return PB_CAPACITY;
+  cudaStream_t s = (cudaStream_t)stream;
+  // scratch: row-major Q8_0 activations, block sums, error words, then the
+  // tensor-core layout for 256 rows
+  const size_t need = 256 * (size_t)(pb::kActStride + pb::kActBlocks * 8 + 8) +
+                      pb::tc_act_bytes(256, pb::kFfn);
+  if (m->op_scratch_bytes < need) {
+    PB_CUDA(cudaStreamSynchronize(s));
+    if (m->op_scratch) PB_CUDA(cudaFree(m->op_scratch));
+    m->op_scratch = nullptr;
+    PB_CUDA(cudaMalloc(&m->op_scratch, need));
+    PB_CUDA(cudaMemset(m->op_scratch, 0, need));
+    m->op_scratch_bytes = need;
+  }
+  if (!m->op_status) {
+    PB_CUDA(cudaMalloc(&m->op_status, 4));
+    PB_CUDA(cudaMemset(m->op_status, 0, 4));
+  }
+  pb::init_kernel_attributes();
+  uint8_t* p = m->op_scratch;
+  pb::Batch b{};
+  b.rows = (int)batch;
+  b.aq = reinterpret_cast<int8_t*>(p);            p += 256 * (size_t)pb::kActStride;
+  b.ad = reinterpret_cast<float*>(p);             p += 256 * (size_t)pb::kActBlocks * 4;
+  b.asum = reinterpret_cast<int*>(p);             p += 256 * (size_t)pb::kActBlocks * 4;
+  b.err = reinterpret_cast<unsigned long long*>(p); p += 256 * 8;
+  PB_CUDA(cudaMemsetAsync(b.err, 0xff, batch * 8, s));
+  const pb::Epilogue ep{pb::EPI_STORE, y, (size_t)mm.rows, nullptr, b.err, 0, 0};
+  if ((int)batch >= pb::kTcMinBatch) {
+    b.aq_tc = reinterpret_cast<int8_t*>(p);
+    b.tc_seqs = 256;
+    pb::launch_quant(b, x, mm.cols, mm.cols, s);
+    pb::TcGemm g{};
+    g.wtype = mm.wtype; g.tiles = mm.image; g.rtiles = mm.rows / 128; g.nb = mm.cols / 32;
+    g.nseg = 1; g.seg[0].rtile_end = g.rtiles; g.seg[0].ep = ep;
+    pb::launch_tc_gemm(g, b, m->op_status, s);
+  } else {
+    pb::launch_quant(b, x, mm.cols, mm.cols, s);
+    pb::launch_qgemv(mm.wtype, mm.w, mm.rows, mm.cols, b, ep, s);
+  }
+  PB_CUDA(cudaGetLastError());
+  return PB_OK;
+}
+
+uint32_t pb_model_matvec_status(pb_model* m, void* stream) {
+  if (!m) return PB_CAPACITY;
+  if (!m->op_status) return PB_OK;
+  unsigned int st = 0;
+  PB_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  PB_CUDA(cudaMemcpy(&st, m->op_status, 4, cudaMemcpyDeviceToHost));
+  if (st) {
+    PB_CUDA(cudaMemset(m->op_status, 0, 4));
+    pb::set_last_error("tensor-core matvec pipeline timed out waiting for an MMA");
+    return PB_DEVICE;
+  }
+  return PB_OK;
+}
+
 uint32_t pb_quantize_q8_device(const float* x, uint32_t rows, uint32_t cols, uint8_t* staging,
                                void* stream) {
   if (cols % 32 || cols > (uint32_t)pb::kFfn || rows == 0) return PB_CAPACITY;

@@ -276,3 +276,28 @@ def test_tensor_core_widest_tile_matches_oracle():
     for b in (0, 63, 64, 300, 511):
         ref = oracle.q4_matvec(w, oracle.prepare_q8(x[b]), rows, cols)
         assert np.array_equal(u32(got[b]), u32(ref)), b
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("batch", [1, 9, 64])
+@pytest.mark.parametrize("layer,role", [(0, 19), (3, 16), (5, 21), (7, 17), (11, 12), (13, 13), (23, 11), (None, 290)])
+def test_model_matvec_matches_oracle(model_view, model_image, layer, role, batch):
+    """pb_model_matvec_device on the model's own tensors (the engine's matvec:
+    CUDA-core below 9 rows, tensor-core tile image from 9) equals the oracle."""
+    from promptboot_b200 import pbtqw25
+    lib = _lib.load()
+    tid = 290 if layer is None else pbtqw25.layer_tensor(layer, role)
+    rows, cols = {19: (896, 896), 16: (128, 896), 21: (128, 896), 17: (896, 896), 12: (4864, 896),
+                  13: (4864, 896), 11: (896, 4864), 290: (151936, 896)}[role]
+    w = pbtqw25.tensor_view(model_image, tid)
+    rng = np.random.default_rng(tid * 10 + batch)
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    y = torch.zeros((batch, rows), dtype=torch.float32, device="cuda")
+    assert lib.pb_model_matvec_device(model_view._h, tid, ptr(dev(x)), batch, ptr(y), None) == 0
+    assert lib.pb_model_matvec_status(model_view._h, None) == 0
+    got = host(y)
+    for b in ([0, batch - 1] if role == 290 else range(batch)):
+        st = oracle.prepare_q8(x[b])
+        ref = oracle.q8_matvec(w, st, rows, cols) if role == 290 else oracle.q4_matvec(w, st, rows, cols)
+        assert np.array_equal(u32(got[b]), u32(ref)), b
+    assert lib.pb_model_matvec_device(model_view._h, 5, ptr(dev(x)), batch, ptr(y), None) != 0  # a norm
