@@ -125,6 +125,10 @@ struct pb_engine {
   int device = 0;
   cudaStream_t stream = nullptr;
   uint32_t max_seqs = 0;
+  // Rows of one forward: the decode batch (max_seqs) or a prefill chunk of
+  // (sequence, prompt position) rows, whichever is larger.
+  uint32_t rows_cap = 0;
+  static constexpr uint32_t kPrefillRows = 512;
   uint32_t capacity = 0;       // positions per slot (KV)
   uint32_t context_limit = 0;  // min(32768, capacity)
   std::vector<Slot> slots;
@@ -414,9 +418,50 @@ struct pb_engine {
       }
     }
     std::vector<int> rs, ps;
-    std::vector<uint32_t> ts, map;
+    std::vector<uint32_t> ts, map, tmap;
     uint32_t first_status = PB_OK;
-    for (uint32_t t = 0; t < len; ++t) {
+    // Every prompt position but the last runs batched: rows are (sequence,
+    // position) pairs, position-major, up to rows_cap per forward.  Each row
+    // evaluates exactly the reference's per-token arithmetic (rows are
+    // independent; attention reads the slot's KV of positions <= its own, all
+    // written by this or an earlier forward).  A row's stage failure faults its
+    // sequence at the earliest failing position (rows of a sequence appear in
+    // increasing position order); later rows of that sequence are discarded.
+    std::vector<uint32_t> base(n);
+    for (uint32_t i = 0; i < n; ++i) base[i] = slots[seq_ids[i]].position;
+    const uint32_t batched = len > 0 ? len - 1 : 0;
+    for (uint32_t t_cur = 0, i_cur = 0; t_cur < batched;) {
+      rs.clear(); ps.clear(); ts.clear(); map.clear(); tmap.clear();
+      while (t_cur < batched && rs.size() < rows_cap) {
+        if (active[i_cur]) {
+          rs.push_back((int)seq_ids[i_cur]);
+          ps.push_back((int)(base[i_cur] + t_cur));
+          ts.push_back(tokens[(size_t)i_cur * len + t_cur]);
+          map.push_back(i_cur);
+          tmap.push_back(t_cur);
+        }
+        if (++i_cur == n) { i_cur = 0; ++t_cur; }
+      }
+      if (rs.empty()) break;
+      uint32_t st = step((uint32_t)rs.size(), rs.data(), ts.data(), ps.data(), false);
+      if (st) return st;
+      for (size_t r = 0; r < rs.size(); ++r) {
+        const uint32_t i = map[r];
+        if (!active[i] || h_err[r] == pb::kNoError) continue;
+        Slot& s = slots[seq_ids[i]];
+        while (s.position < base[i] + tmap[r]) advance(s);
+        errs[i] = fault(s, stage_error(h_err[r], s.position), n == 1 ? host_logits : nullptr);
+        active[i] = 0;
+        if (!first_status) first_status = errs[i].status;
+      }
+    }
+    for (uint32_t i = 0; i < n; ++i) {
+      if (!active[i]) continue;
+      Slot& s = slots[seq_ids[i]];
+      while (s.position < base[i] + batched) advance(s);
+    }
+    // The last prompt position of every sequence: one forward with logits.
+    for (uint32_t t = batched; t < len; ++t) {
       rs.clear(); ps.clear(); ts.clear(); map.clear();
       for (uint32_t i = 0; i < n; ++i) {
         if (!active[i]) continue;
@@ -514,29 +559,31 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   e->context_limit = std::min<uint32_t>(PB_CONTEXT_LIMIT, max_context);
   e->slots.resize(max_seqs);
   const size_t S = max_seqs;
+  e->rows_cap = std::max<uint32_t>(max_seqs, pb_engine::kPrefillRows);
+  const size_t R = e->rows_cap;
   cudaError_t c = cudaSetDevice(e->device);
   auto chk = [&](cudaError_t r) { if (c == cudaSuccess) c = r; };
   chk(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   chk(dalloc(&e->kv, S * (size_t)max_context * 6144));
   chk(dalloc(&e->history, S * (size_t)max_context));
-  chk(dalloc(&e->hidden, S * 896));
-  chk(dalloc(&e->q, S * 896));
-  chk(dalloc(&e->k, S * 128));
-  chk(dalloc(&e->v, S * 128));
-  chk(dalloc(&e->attn, S * 896));
-  chk(dalloc(&e->gate, S * 4864));
-  chk(dalloc(&e->up, S * 4864));
+  chk(dalloc(&e->hidden, R * 896));
+  chk(dalloc(&e->q, R * 896));
+  chk(dalloc(&e->k, R * 128));
+  chk(dalloc(&e->v, R * 128));
+  chk(dalloc(&e->attn, R * 896));
+  chk(dalloc(&e->gate, R * 4864));
+  chk(dalloc(&e->up, R * 4864));
   chk(dalloc(&e->logits, S * 151936));
-  chk(dalloc(&e->scores, S * 14 * ((size_t)max_context + 4)));
-  chk(dalloc(&e->aq, S * 4864));
-  chk(dalloc(&e->ad, S * 152));
-  chk(dalloc(&e->asum, S * 152));
-  e->tc_seqs = (int)((S + 63) / 64 * 64);
+  chk(dalloc(&e->scores, R * 14 * ((size_t)max_context + 4)));
+  chk(dalloc(&e->aq, R * 4864));
+  chk(dalloc(&e->ad, R * 152));
+  chk(dalloc(&e->asum, R * 152));
+  e->tc_seqs = (int)((R + 63) / 64 * 64);
   chk(dalloc(&e->aq_tc, pb::tc_act_bytes(e->tc_seqs, 4864)));
-  chk(dalloc(&e->d_slots, S));
-  chk(dalloc(&e->d_positions, S));
-  chk(dalloc(&e->d_tokens, S));
-  chk(dalloc(&e->d_err, S * pb_engine::kErrSteps));
+  chk(dalloc(&e->d_slots, R));
+  chk(dalloc(&e->d_positions, R));
+  chk(dalloc(&e->d_tokens, R));
+  chk(dalloc(&e->d_err, std::max(R, S * pb_engine::kErrSteps)));
   chk(dalloc(&e->d_greedy, S));
   chk(dalloc(&e->d_greedy_bits, S));
   chk(dalloc(&e->d_states, S * 2));
@@ -547,10 +594,10 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   chk(dalloc(&e->d_token_log, S * pb_engine::kErrSteps));
   chk(dalloc(&e->d_tc_status, 1));
   chk(cudaMallocHost(&e->h_tc_status, 4));
-  chk(cudaMallocHost(&e->h_slots, S * 4));
-  chk(cudaMallocHost(&e->h_positions, S * 4));
-  chk(cudaMallocHost(&e->h_tokens, S * 4));
-  chk(cudaMallocHost(&e->h_err, S * 8 * pb_engine::kErrSteps));
+  chk(cudaMallocHost(&e->h_slots, R * 4));
+  chk(cudaMallocHost(&e->h_positions, R * 4));
+  chk(cudaMallocHost(&e->h_tokens, R * 4));
+  chk(cudaMallocHost(&e->h_err, 8 * std::max(R, S * pb_engine::kErrSteps)));
   chk(cudaMallocHost(&e->h_greedy, S * 4));
   chk(cudaMallocHost(&e->h_greedy_bits, S * 4));
   if (c == cudaSuccess) pb::init_kernel_attributes();

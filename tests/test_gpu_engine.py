@@ -255,3 +255,36 @@ def test_tensor_core_up_stage_fault_matches_cuda_core_path(model_image):
             assert t[6] == t1[6]
     e12.close()
     view.close()
+
+
+def test_batched_prefill_faults_each_sequence_at_its_position(model_image):
+    """Prompt positions but the last run as one batched forward of (sequence,
+    position) rows.  A NaN embedding scale of token 777 faults each sequence at
+    the EMBEDDING stage of the position where 777 first appears (0, 3, or the
+    last position 7); a sequence without it still matches the oracle."""
+    img = model_image.copy()
+    off = int(np.frombuffer(img[pbtqw25.TENSOR_DIR + 0 * 96 + 32:][:8].tobytes(), np.uint64)[0])
+    blk = off + 777 * 28 * 18
+    img[blk:blk + 2] = np.frombuffer(np.uint16(0x7E00).tobytes(), np.uint8)
+    view = api.ModelView(img)
+    n, plen = 4, 8
+    prompts = np.stack([prompt(plen, seed=700 + i) for i in range(n)])
+    prompts[prompts == 777] = 778
+    prompts[1, 3] = 777
+    prompts[1, 5] = 777
+    prompts[2, 0] = 777
+    prompts[3, 7] = 777
+    e = api.InferenceEngine(view, max_seqs=n, max_context=64)
+    status, steps, errs = e.prefill_batch(np.arange(n), prompts, 4)
+    assert status == 6
+    assert errs[0].status == 0
+    for i, p in [(1, 3), (2, 0), (3, 7)]:
+        t = errs[i].tuple()
+        assert t[:6] == [6, 3, NO, p, 0, 0] and t[7] == (7 << 32) | 0, (i, t)
+        assert t[6] & 0x7F800000 == 0x7F800000 and t[6] & 0x7FFFFF
+        assert e.usage(i).state == 3
+    ref, _ = oracle_prefill_logits(model_image, prompts[0])
+    assert np.array_equal(e.logits(0), ref.view(np.uint32))
+    assert steps[0].selected_token == oracle.argmax(ref) and steps[0].position == plen
+    e.close()
+    view.close()

@@ -301,3 +301,25 @@ def test_model_matvec_matches_oracle(model_view, model_image, layer, role, batch
         ref = oracle.q8_matvec(w, st, rows, cols) if role == 290 else oracle.q4_matvec(w, st, rows, cols)
         assert np.array_equal(u32(got[b]), u32(ref)), b
     assert lib.pb_model_matvec_device(model_view._h, 5, ptr(dev(x)), batch, ptr(y), None) != 0  # a norm
+
+
+@pytest.mark.parametrize("position", [31023, 20001])
+def test_attention_long_context_matches_oracle(position):
+    """Config 4 scale (SURVEY: 30,000-token prompts + 1,024 decode steps, up to
+    31,024 positions): the global-scores attention path over a seeded KV of
+    slot 0, layer 0, against the oracle."""
+    lib = _lib.load()
+    cap = 31024
+    rng = np.random.default_rng(position)
+    kv = rng.standard_normal(4 * cap * 64).astype(np.float32)   # slot 0, layer 0 only
+    q = rng.standard_normal((1, 896)).astype(np.float32)
+    out = torch.zeros((1, 896), dtype=torch.float32, device="cuda")
+    pos = np.array([position], dtype=np.uint32)
+    assert lib.pb_attention_device(ptr(dev(q)), ptr(dev(kv)), cap, 0,
+                                   pos.ctypes.data_as(ctypes.c_void_p), 1, 0, ptr(out), None,
+                                   None) == 0
+    sync()
+    full = np.zeros(24 * 4 * cap * 64, dtype=np.float32)
+    full[:kv.size] = kv
+    ref, _ = oracle.attention(q[0], full, cap, 0, position, (position + 4) & ~3)
+    assert np.array_equal(u32(host(out)[0]), u32(ref))
