@@ -101,8 +101,16 @@ rmsnorm_quant_kernel(Batch b, const float* __restrict__ weight, uint32_t layer_o
       hi = max(hi, ext[1][w]);
     }
     if (hi == 255 || (hi >= lo && hi - lo > 19)) {
+      // index order; the loads and widenings run ahead of the f64 add chain
       double serial = 0.0;
-      for (int e = 0; e < kHidden; ++e) serial += (double)sq[e];
+#pragma unroll 8
+      for (int e = 0; e < kHidden; e += 4) {
+        const float4 t4 = *reinterpret_cast<const float4*>(&sq[e]);
+        serial += (double)t4.x;
+        serial += (double)t4.y;
+        serial += (double)t4.z;
+        serial += (double)t4.w;
+      }
       tree = serial;
     }
     total = tree;

@@ -56,7 +56,8 @@ struct Batch {
   float* product_out = nullptr;  // optional [B][4864] SwiGLU output (operator API)
   int span_min = 0;              // minimum softmax span (operator API; 0 = natural)
   float* probs_out = nullptr;    // optional [B][14][score_stride] final probabilities
-  // Tensor-core activation layout, written by the quantizers when aq_tc is set,
+  // Tensor-core activation layout, written by the quantizers when aq_tc is set
+  // (instead of the row-major aq/ad/asum),
   // chunk-major (4 Q-blocks per chunk) so one chunk of one sequence tile is one
   // contiguous copy: [K / 128][tc_seqs / 8][kTcGroupBytes], each 8-sequence
   // group = 4 blocks x 256 B of quants (bytes 0-15 of the 8 rows, then bytes

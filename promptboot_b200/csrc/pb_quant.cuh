@@ -24,19 +24,25 @@ __device__ __forceinline__ int warp_sum_i32(int v) {
 
 // fp32_sse2.rs:945-983, one warp per 32-element block: d = amax / 127 rounded to
 // binary16 for storage, inverse from the unrounded d, q = trunc(x * inv +- 0.5).
-// The block's quant sum is kept for the Q4_0 zero-point correction.
-__device__ __forceinline__ int quantize_block_warp(float x, int8_t* aq, float* ad, int* asum,
-                                                   float& dstored) {
+// Returns this lane's quant; dstored = the stored scale (binary16 value as f32).
+__device__ __forceinline__ int quantize_lane(float x, float& dstored) {
   float amax = warp_max_f32(fbits(bitsf(x) & 0x7fffffffu));
   float d = __fdiv_rn(amax, 127.0f);
   float inverse = bitsf(d) == 0 ? 0.0f : __fdiv_rn(1.0f, d);
   float v = __fmul_rn(x, inverse);
   float half = (bitsf(v) >> 31) == 0 ? 0.5f : -0.5f;
-  int q = __float2int_rz(__fadd_rn(v, half));
-  int lane = threadIdx.x & 31;
-  aq[lane] = (int8_t)q;
-  int total = warp_sum_i32((int)(int8_t)q);
   dstored = half_to_f32(f32_to_half(bitsf(d)));
+  return __float2int_rz(__fadd_rn(v, half));
+}
+
+// Row-major Q8_0 activation (the CUDA-core matvec's input): quants, scale and
+// the block's quant sum for the Q4_0 zero-point correction.
+__device__ __forceinline__ int quantize_block_warp(float x, int8_t* aq, float* ad, int* asum,
+                                                   float& dstored) {
+  const int q = quantize_lane(x, dstored);
+  const int lane = threadIdx.x & 31;
+  aq[lane] = (int8_t)q;
+  const int total = warp_sum_i32((int)(int8_t)q);
   if (lane == 0) {
     *ad = dstored;
     *asum = total;
@@ -44,21 +50,23 @@ __device__ __forceinline__ int quantize_block_warp(float x, int8_t* aq, float* a
   return q;
 }
 
-// Row `row`, block `blk` of a K = 32 * nb activation: quantizes into the
-// row-major buffers and, when the batch carries them, the tensor-core layout.
+// Row `row`, block `blk` of an activation: the tensor-core layout when the batch
+// carries one (Batch::aq_tc: chunk-major group (blk / 4, row / 8), quants of
+// block blk % 4 at 256 (blk % 4), its scales after the 4 blocks), else the
+// row-major buffers.
 __device__ __forceinline__ void quantize_row_block(const Batch& b, float x, int row, int blk) {
   float d;
-  const int q = quantize_block_warp(x, b.aq + (size_t)row * kActStride + blk * 32,
-                                    b.ad + (size_t)row * kActBlocks + blk,
-                                    b.asum + (size_t)row * kActBlocks + blk, d);
   if (b.aq_tc) {
-    // Chunk-major tensor-core layout (Batch::aq_tc): group (blk / 4, row / 8),
-    // quants of block blk % 4 at 256 (blk % 4), its scales after the 4 blocks.
+    const int q = quantize_lane(x, d);
     const int lane = threadIdx.x & 31;
     const int j = blk & 3;
     int8_t* grp = b.aq_tc + ((size_t)(blk >> 2) * (b.tc_seqs >> 3) + (row >> 3)) * kTcGroupBytes;
     grp[j * 256 + (lane >> 4) * 128 + (row & 7) * 16 + (lane & 15)] = (int8_t)q;
     if (lane == 0) reinterpret_cast<float*>(grp + 1024)[j * 8 + (row & 7)] = d;
+  } else {
+    quantize_block_warp(x, b.aq + (size_t)row * kActStride + blk * 32,
+                        b.ad + (size_t)row * kActBlocks + blk,
+                        b.asum + (size_t)row * kActBlocks + blk, d);
   }
 }
 
