@@ -262,7 +262,7 @@ struct TcCfg {
   static_assert((kCols & (kCols - 1)) == 0 && kCols >= 32, "TMEM allocation size");
   static_assert(kPerSm * (kBytes + 1024) <= 233472, "shared memory per SM");
 };
-using Cfg8 = TcCfg<16, 8, 3, 3, 2, 8>;
+using Cfg8 = TcCfg<16, 8, 2, 5, 2, 8>;
 using Cfg16 = TcCfg<16, 8, 2, 4, 4>;
 using Cfg32 = TcCfg<32, 16, 2, 4, 2>;
 using Cfg64 = TcCfg<64, 16, 1, 6, 2>;
