@@ -130,12 +130,14 @@ PB_API uint32_t pb_engine_reset_to_prefix(pb_engine *engine, uint32_t seq, uint3
 PB_API uint32_t pb_engine_usage(pb_engine *engine, uint32_t seq, pb_usage *out);
 PB_API uint32_t pb_engine_position(pb_engine *engine, uint32_t seq);
 
-/* Batched forms: one forward step over n sequences at their own positions.
- * prefill_batch runs `len` prompt tokens per sequence (tokens is [n][len]) in
- * lockstep; decode_batch evaluates tokens[i] for seqs[i] (require_greedy = 1 is
- * decode, 0 is decode_selected).  Per-sequence results land in steps[i]/errs[i];
- * the call returns PB_OK when every sequence succeeded, else the first failing
- * status.  Logits stay on the device (row i = seqs[i]); see pb_engine_logits. */
+/* Batched forms: one forward step over n distinct sequences at their own
+ * positions (a sequence listed twice: PB_CAPACITY).  prefill_batch runs `len`
+ * prompt tokens per sequence (tokens is [n][len]; positions but the last as
+ * batched (sequence, position) rows, results as the token-serial reference);
+ * decode_batch evaluates tokens[i] for seqs[i] (require_greedy = 1 is decode, 0
+ * is decode_selected).  Per-sequence results land in steps[i]/errs[i]; the call
+ * returns PB_OK when every sequence succeeded, else the first failing status.
+ * Logits stay on the device (row i = seqs[i]); see pb_engine_logits. */
 PB_API uint32_t pb_engine_prefill_batch(pb_engine *engine, uint32_t n, const uint32_t *seqs,
                                  const uint32_t *tokens, uint32_t len,
                                  uint32_t generation_reserve, pb_step *steps, pb_error *errs);

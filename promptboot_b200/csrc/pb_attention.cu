@@ -52,7 +52,7 @@ struct AttnSmem {
 };
 
 __global__ void __launch_bounds__(kThreads, 4)
-attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize) {
+attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize, const float* rope) {
   pdl_begin();
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;
@@ -72,8 +72,48 @@ attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize) {
   float* score = sc + h * span_cap;
 
   const float* qg = b.q + (size_t)row * kHidden + kh * kHeadsPerKv * 64;
-  qs[tid] = qg[tid];
-  qs[tid + kThreads] = qg[tid + kThreads];
+  if (rope) {
+    // RoPE and the KV write of this step's position (fp32_sse2.rs:1413-1428,
+    // inference.rs:1809-1887), for this CTA's 7 query heads and its KV head:
+    // lane `pair` of warp h rotates (pair, pair + 32) of head 7 kh + h; warp 0
+    // also rotates K head kh and writes it, warps 0-1 write V head kh.  Only
+    // valid when no other row of the launch shares the slot (decode steps).
+    const int position = positions - 1;
+    const uint32_t ord = (uint32_t)layer + 1;
+    const float* table = rope + (size_t)position * 64;
+    const float c = table[lane * 2], sn = table[lane * 2 + 1];
+    {
+      const float left = qg[h * 64 + lane], right = qg[h * 64 + lane + 32];
+      const float l2 = __fsub_rn(__fmul_rn(left, c), __fmul_rn(right, sn));
+      const float r2 = __fadd_rn(__fmul_rn(left, sn), __fmul_rn(right, c));
+      qs[h * 64 + lane] = l2;
+      qs[h * 64 + lane + 32] = r2;
+      const int qi = (kh * kHeadsPerKv + h) * 64 + lane;
+      check_finite(l2, &b.err[row], ord, D_ROPE, 0, qi);
+      check_finite(r2, &b.err[row], ord, D_ROPE, 0, qi + 32);
+    }
+    float* kvs = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
+    if (h == 0) {
+      const float* kg = b.k + (size_t)row * 128 + kh * 64;
+      const float left = kg[lane], right = kg[lane + 32];
+      const float l2 = __fsub_rn(__fmul_rn(left, c), __fmul_rn(right, sn));
+      const float r2 = __fadd_rn(__fmul_rn(left, sn), __fmul_rn(right, c));
+      check_finite(l2, &b.err[row], ord, D_ROPE, 1, kh * 64 + lane);
+      check_finite(r2, &b.err[row], ord, D_ROPE, 1, kh * 64 + lane + 32);
+      check_finite(l2, &b.err[row], ord, D_KV, 0, kh * 64 + lane);
+      check_finite(r2, &b.err[row], ord, D_KV, 0, kh * 64 + lane + 32);
+      kvs[kv_key_word(cap, layer, kh, position, lane)] = l2;
+      kvs[kv_key_word(cap, layer, kh, position, lane + 32)] = r2;
+    } else if (h <= 2) {
+      const int cc = (h - 1) * 32 + lane;
+      kvs[kv_value_word(cap, layer, kh, position, cc)] = b.v[(size_t)row * 128 + kh * 64 + cc];
+    }
+    __threadfence();  // the cp.async reads below go through L2
+    __syncthreads();
+  } else {
+    qs[tid] = qg[tid];
+    qs[tid + kThreads] = qg[tid + kThreads];
+  }
 
   // Chunk t = K tiles 16t .. 16t + 15, each 1 KB contiguous in the cache.
   auto load_k = [&](int t, float* dst) {
@@ -207,7 +247,8 @@ attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize) {
 
 int attention_smem_positions() { return kAttnMaxPositions; }
 
-void launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, cudaStream_t s) {
+void launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
+                              cudaStream_t s) {
   const size_t bytes = AttnSmem::bytes(span_cap);
   static size_t configured = 0;  // one device per process
   if (bytes > configured) {
@@ -215,7 +256,8 @@ void launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quan
                          (int)AttnSmem::bytes(kAttnMaxPositions));
     configured = AttnSmem::bytes(kAttnMaxPositions);
   }
-  launch_pdl(attention_kv_group_kernel, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
+  launch_pdl(attention_kv_group_kernel, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize,
+             rope);
 }
 
 }  // namespace pb

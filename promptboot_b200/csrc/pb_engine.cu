@@ -255,8 +255,10 @@ struct pb_engine {
 
   // Enqueues one forward step for rows already staged in d_slots/d_positions/
   // d_tokens; stage failures land in err[0..rows).
+  // distinct_slots: no two rows share a slot (decode); RoPE and the KV write
+  // then run inside the attention launch.
   void enqueue_forward(uint32_t rows, bool want_logits, unsigned long long* err,
-                       bool want_greedy = true) {
+                       bool want_greedy = true, bool distinct_slots = true) {
     using namespace pb;
     const pb_model* m = model;
     Batch b = batch(rows, err);
@@ -272,8 +274,12 @@ struct pb_engine {
       const Epilogue ev{EPI_BIAS, v, 128, reinterpret_cast<const float*>(T(20)), err, ord, D_V};
       matvec(W_Q4_0, b, 896, m->tc + m->tc_qkv[layer],
              {{T(19), 896, eq}, {T(16), 128, ek}, {T(21), 128, ev}}, PB_KC_GEMV);
-      PB_LAUNCH(PB_KC_ROPE_KV, launch_rope_kv(b, layer, m->rope, stream));
-      PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, max_span, true, stream));
+      if (distinct_slots) {
+        PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, max_span, true, m->rope, stream));
+      } else {
+        PB_LAUNCH(PB_KC_ROPE_KV, launch_rope_kv(b, layer, m->rope, stream));
+        PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, max_span, true, nullptr, stream));
+      }
       const Epilogue eo{EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_ATTN_OUTPUT};
       matvec(W_Q4_0, b, 896, m->tc + m->tc_o[layer], {{T(17), 896, eo}}, PB_KC_GEMV);
       PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(T(14)), ord,
@@ -300,7 +306,7 @@ struct pb_engine {
   // One synchronous step over explicit rows; fills per-row stage errors (~0 = ok)
   // and, with logits, greedy ids/bits in h_greedy/h_greedy_bits.
   uint32_t step(uint32_t rows, const int* slot_ids, const uint32_t* toks, const int* pos,
-                bool want_logits) {
+                bool want_logits, bool distinct_slots = true) {
     std::copy(slot_ids, slot_ids + rows, h_slots);
     std::copy(toks, toks + rows, h_tokens);
     std::copy(pos, pos + rows, h_positions);
@@ -309,7 +315,7 @@ struct pb_engine {
     PB_CUDA(cudaMemcpyAsync(d_positions, h_positions, rows * 4, cudaMemcpyHostToDevice, stream));
     max_span = 4;
     for (uint32_t i = 0; i < rows; ++i) max_span = std::max(max_span, (pos[i] + 4) & ~3);
-    enqueue_forward(rows, want_logits, d_err);
+    enqueue_forward(rows, want_logits, d_err, true, distinct_slots);
     PB_CUDA(cudaGetLastError());
     PB_CUDA(cudaMemcpyAsync(h_err, d_err, rows * 8, cudaMemcpyDeviceToHost, stream));
     PB_CUDA(cudaMemcpyAsync(h_tc_status, d_tc_status, 4, cudaMemcpyDeviceToHost, stream));
@@ -443,7 +449,9 @@ struct pb_engine {
         if (++i_cur == n) { i_cur = 0; ++t_cur; }
       }
       if (rs.empty()) break;
-      uint32_t st = step((uint32_t)rs.size(), rs.data(), ts.data(), ps.data(), false);
+      // rows of one sequence at several positions: the KV writes of all rows
+      // must land before any row's attention (separate RoPE/KV launch)
+      uint32_t st = step((uint32_t)rs.size(), rs.data(), ts.data(), ps.data(), false, false);
       if (st) return st;
       for (size_t r = 0; r < rs.size(); ++r) {
         const uint32_t i = map[r];
@@ -533,6 +541,18 @@ struct pb_engine {
 namespace {
 
 bool seq_ok(const pb_engine* e, uint32_t seq) { return e && seq < e->max_seqs; }
+
+// The batched entry points evaluate one row per listed sequence; a sequence
+// listed twice would have two rows write the same KV position.
+bool distinct_seqs(const pb_engine* e, uint32_t n, const uint32_t* seqs) {
+  std::vector<char> seen(e->max_seqs, 0);
+  for (uint32_t i = 0; i < n; ++i) {
+    if (seqs[i] >= e->max_seqs) continue;  // reported per sequence by the caller
+    if (seen[seqs[i]]) return false;
+    seen[seqs[i]] = 1;
+  }
+  return true;
+}
 
 pb_error bad_seq(uint32_t seq, uint32_t max) {
   return make_error(PB_CAPACITY, DOM_PROMPT, NO_LAYER, 0, NO_TENSOR, max, seq, K_STATE, 7);
@@ -700,6 +720,7 @@ uint32_t pb_engine_decode_batch(pb_engine* e, uint32_t n, const uint32_t* seqs,
                                 const uint32_t* tokens, uint32_t require_greedy, pb_step* steps,
                                 pb_error* errs) {
   if (!e || n == 0 || n > e->max_seqs) return PB_CAPACITY;
+  if (!distinct_seqs(e, n, seqs)) return PB_CAPACITY;
   cudaSetDevice(e->device);
   std::vector<int> rs, ps;
   std::vector<uint32_t> ts, map;
@@ -766,6 +787,7 @@ uint32_t pb_engine_prefill_batch(pb_engine* e, uint32_t n, const uint32_t* seqs,
                                  const uint32_t* tokens, uint32_t len, uint32_t reserve,
                                  pb_step* steps, pb_error* errs) {
   if (!e || n == 0 || n > e->max_seqs) return PB_CAPACITY;
+  if (!distinct_seqs(e, n, seqs)) return PB_CAPACITY;
   cudaSetDevice(e->device);
   std::vector<char> active(n, 0);
   uint32_t first = PB_OK;
@@ -849,7 +871,7 @@ static void sampler_error(pb_error* err, const pb::SamplerRow& r, uint64_t count
 
 uint32_t pb_engine_sample(pb_engine* e, uint32_t n, const uint32_t* seqs,
                           pb_sampling_state* states, uint32_t* ids, pb_error* errs) {
-  if (!e || n == 0 || n > e->last_rows) return PB_CAPACITY;
+  if (!e || n == 0 || n > e->last_rows || !distinct_seqs(e, n, seqs)) return PB_CAPACITY;
   cudaSetDevice(e->device);
   std::vector<uint64_t> off(n);
   std::vector<uint32_t> len(n);
@@ -890,7 +912,7 @@ uint32_t pb_engine_sample(pb_engine* e, uint32_t n, const uint32_t* seqs,
 uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
                             pb_sampling_state* states, uint32_t steps, uint32_t* out_tokens,
                             pb_error* errs) {
-  if (!e || n == 0 || n > e->last_rows) return PB_CAPACITY;
+  if (!e || n == 0 || n > e->last_rows || !distinct_seqs(e, n, seqs)) return PB_CAPACITY;
   cudaSetDevice(e->device);
   for (uint32_t i = 0; i < n; ++i) {
     if (!seq_ok(e, seqs[i])) return PB_CAPACITY;

@@ -418,11 +418,13 @@ __global__ void attention_kernel(Batch b, int layer) {
   }
 }
 
-void launch_attention(const Batch& b, int layer, int max_span, bool quantize, cudaStream_t s) {
+void launch_attention(const Batch& b, int layer, int max_span, bool quantize, const float* rope,
+                      cudaStream_t s) {
   if (max_span <= kAttnMaxPositions) {
-    launch_attention_grouped(b, layer, (max_span + 3) & ~3, quantize, s);
+    launch_attention_grouped(b, layer, (max_span + 3) & ~3, quantize, rope, s);
     return;
   }
+  if (rope) launch_rope_kv(b, layer, rope, s);
   launch_pdl(attention_kernel, b.rows * kQHeads, 256, 0, s, b, layer);
   if (quantize) launch_quant(b, b.attn, kHidden, kHidden, s);
 }

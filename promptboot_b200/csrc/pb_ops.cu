@@ -466,7 +466,7 @@ uint32_t pb_attention_device(const float* q, const float* kv, uint32_t capacity,
   b.q = const_cast<float*>(q); b.kv = const_cast<float*>(kv); b.capacity = capacity;
   b.attn = out; b.scores = sc; b.score_stride = span_max; b.span_min = (int)span;
   b.probs_out = scores;
-  pb::launch_attention(b, (int)layer, (int)span_max, false, s);
+  pb::launch_attention(b, (int)layer, (int)span_max, false, nullptr, s);
   PB_CUDA(cudaGetLastError());
   if (!scores) PB_CUDA(cudaFreeAsync(sc, s));
   return PB_OK;

@@ -28,6 +28,12 @@ __device__ __forceinline__ uint32_t order_key(float v) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Inverse of order_key on the key's high word.
+__device__ __forceinline__ float key_value(unsigned long long key) {
+  const uint32_t k = (uint32_t)(key >> 32);
+  return fbits((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 __device__ __forceinline__ float penalize(float v) {
   uint32_t s = bitsf(v);
   return ((s & 0x80000000u) && (s & 0x7fffffffu)) ? __fmul_rn(v, fbits(0x3f8ccccdu))
@@ -78,7 +84,58 @@ __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t*
   const int start = warp * seg;
   const int end = min(words, start + seg);
   unsigned long long entry = 0, thr = 0;
-  for (int base = start; base < end; base += 128) {
+  // Float image of the list's K-th key: a penalty only lowers a value (x/1.1
+  // for x >= 0, 1.1x for x < 0, zeros unchanged), so a raw value below it can
+  // never enter the list and skips the key work; equal values go on to the
+  // exact (value, id) key comparison.  Non-finite values always go on (they are
+  // recorded as the row's first non-finite word).
+  float thr_f = fbits(0xff800000u);
+  auto offer = [&](float val, int i) {
+    const uint32_t vb = bitsf(val);
+    const bool nonfinite = !finite_bits(vb);
+    const bool cand = i < end && (val >= thr_f || nonfinite);
+    if (__ballot_sync(kFull, cand) == 0) return;
+    unsigned long long key = 0;
+    if (cand) {
+      if (nonfinite) atomicMin(bad, ((unsigned long long)i << 32) | vb);
+      if (penal && (penal[i >> 5] >> (i & 31) & 1u)) val = penalize(val);
+      key = make_key(val, (uint32_t)i);
+    }
+    list_offer<K>(entry, thr, key, lane);
+    thr_f = thr == 0 ? fbits(0xff800000u) : key_value(thr);
+  };
+  // Software pipeline: the next four 512-byte loads of the warp are in flight
+  // while the current four are ranked.
+  constexpr int kBatch = 4;
+  int base = start;
+  if (base + kBatch * 128 <= end) {
+    float4 cur[kBatch], nxt[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      cur[u] = *reinterpret_cast<const float4*>(x + base + u * 128 + lane * 4);
+    for (;;) {
+      const int next = base + kBatch * 128;
+      const bool more = next + kBatch * 128 <= end;
+      if (more) {
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+          nxt[u] = *reinterpret_cast<const float4*>(x + next + u * 128 + lane * 4);
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i0 = base + u * 128 + lane * 4;
+        offer(cur[u].x, i0);
+        offer(cur[u].y, i0 + 1);
+        offer(cur[u].z, i0 + 2);
+        offer(cur[u].w, i0 + 3);
+      }
+      base = next;
+      if (!more) break;
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) cur[u] = nxt[u];
+    }
+  }
+  for (; base < end; base += 128) {
     const int i0 = base + lane * 4;
     float v[4];
     if (i0 + 3 < end) {
@@ -89,18 +146,7 @@ __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t*
       for (int j = 0; j < 4; ++j) v[j] = (i0 + j < end) ? x[i0 + j] : 0.0f;
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int i = i0 + j;
-      unsigned long long key = 0;
-      if (i < end) {
-        float val = v[j];
-        uint32_t vb = bitsf(val);
-        if (!finite_bits(vb)) atomicMin(bad, ((unsigned long long)i << 32) | vb);
-        if (penal && (penal[i >> 5] >> (i & 31) & 1u)) val = penalize(val);
-        key = make_key(val, (uint32_t)i);
-      }
-      list_offer<K>(entry, thr, key, lane);
-    }
+    for (int j = 0; j < 4; ++j) offer(v[j], i0 + j);
   }
   if (lane < K) warp_keys[warp * K + lane] = entry;
   __syncthreads();
@@ -195,13 +241,15 @@ sampler_kernel(float* logits, size_t ld, int words, const uint32_t* __restrict__
   const uint32_t random24 = (uint32_t)((state * 0x2545f4914f6cdd1dull) >> 40);
 
   // fp32_sse2.rs:1818-1845
+  // The ranked (penalised) values come back from the keys (order_key is
+  // invertible up to -0 -> +0, which no result below can distinguish).
   uint32_t ids[20];
   float weights[20];
-  const float maximum = x[(uint32_t)~(uint32_t)top[0]];
+  const float maximum = key_value(top[0]);
   double total = 0.0;
   for (int at = 0; at < 20; ++at) {
     ids[at] = ~(uint32_t)top[at];
-    float v = x[ids[at]];
+    float v = key_value(top[at]);
     weights[at] = expf_ref(__fdiv_rn(__fsub_rn(v, maximum), fbits(0x3f333333u)));
     total += (double)weights[at];
   }

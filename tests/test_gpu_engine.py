@@ -288,3 +288,19 @@ def test_batched_prefill_faults_each_sequence_at_its_position(model_image):
     assert steps[0].selected_token == oracle.argmax(ref) and steps[0].position == plen
     e.close()
     view.close()
+
+
+def test_batched_calls_reject_a_sequence_listed_twice(model_image):
+    """Two rows of one slot would write the same KV position: the batched entry
+    points refuse duplicates with PB_CAPACITY before touching any state."""
+    view = api.ModelView(model_image)
+    e = api.InferenceEngine(view, max_seqs=4, max_context=32)
+    seqs = np.array([0, 1, 0], dtype=np.uint32)
+    st, _, _ = e.prefill_batch(seqs, np.stack([prompt(3, seed=i) for i in range(3)]), 4)
+    assert st == 4 and e.position(0) == 0 and e.position(1) == 0
+    st, _, _ = e.prefill_batch(np.array([0, 1], dtype=np.uint32), np.stack([prompt(3), prompt(3, 9)]), 4)
+    assert st == 0
+    st, _, _ = e.decode_batch(seqs, np.array([1, 2, 3], dtype=np.uint32))
+    assert st == 4 and e.position(0) == 3
+    e.close()
+    view.close()
