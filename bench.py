@@ -50,7 +50,8 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=8)
     p.add_argument("--cpu-tokens", type=int, default=6, help="CPU-baseline tokens per thread")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--op", choices=["attention", "qmatvec", "matvec-sweep", "sampler"], default=None,
+    p.add_argument("--op", choices=["attention", "qmatvec", "matvec-sweep", "sampler", "decode1"],
+                   default=None,
                    help="time one operator on synthetic inputs (the small cases of the ncu "
                         "captures under profiles/) instead of the decode bench")
     p.add_argument("--op-rows", type=int, default=192, help="--op: sequences")
@@ -109,6 +110,45 @@ def run_matvec_sweep(args):
     print(json.dumps({"op": "matvec-sweep", "config": "config 2 linear sweep", "peak_GB_s": hbm,
                       "peak_source": peak_kind, "l2": "256 MB write between timed calls",
                       "cases": out}), flush=True)
+
+
+def run_decode_single(args):
+    """Config 0 (single sequence): 64-token prompt (default_rng(0x5eed0000)),
+    batched prefill, then 64 sampled decode steps with seed 1 through the
+    device-resident generate loop (sample -> decode_selected), timed with CUDA
+    events on the engine stream."""
+    import ctypes
+    import torch
+    from promptboot_b200 import _lib, api, pbtqw25, shard
+    lib = _lib.load()
+    img = pbtqw25.load_or_synthesize(0)
+    view = api.ModelView(img)
+    eng = api.InferenceEngine(view, max_seqs=1, max_context=256)
+    prompt = shard.prompt_for(0, 64)
+    stream = torch.cuda.ExternalStream(lib.pb_engine_stream(eng._h))
+    t0 = time.perf_counter()
+    logits = np.zeros(api.VOCAB, dtype=np.uint32)
+    eng.prefill(prompt, 128, logits)
+    prefill_s = time.perf_counter() - t0
+    state = api.SamplingState(1)
+    st, _, _ = eng.generate([0], [state], 4, want_tokens=False)   # warm-up
+    assert st == 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    st, toks, _ = eng.generate([0], [state], 64)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    assert st == 0
+    ms = e0.elapsed_time(e1)
+    eng.close()
+    view.close()
+    print(json.dumps({"op": "decode1", "config": "config 0 single sequence", "prompt": 64,
+                      "decode_steps": 64, "tok_s": round(64 / (ms / 1000.0), 1),
+                      "ms_per_token": round(ms / 64, 3), "prefill_ms_64_tokens": round(prefill_s * 1000, 1),
+                      "hbm_bytes_per_token": 346206720,
+                      "hbm_frac": round(346206720 / (ms / 64 / 1000) / 1e9 / measured_peaks()[0], 3)}),
+          flush=True)
 
 
 def run_sampler_batch(args):
@@ -503,6 +543,9 @@ def main():
         return
     if args.op == "sampler":
         run_sampler_batch(args)
+        return
+    if args.op == "decode1":
+        run_decode_single(args)
         return
     if args.op:
         run_op(args)
