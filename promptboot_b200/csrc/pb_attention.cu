@@ -9,15 +9,24 @@
 //   sum = sum over 4-groups IN ORDER of f64(fl(fl(e0+e1) + fl(e2+e3)))   one lane per head
 //   prob = fl(e * f32(1.0 / sum))
 //   out[h][c] = f32(sum_p f64(fl(prob[h][p] * v[p][c])))              p in order
-// 224 threads = one warp per query head, so q and the probabilities are warp
-// broadcasts and the softmax needs no block barrier.  K arrives in the
-// reference's 4-position tiles ([component][4 positions], 1 KB) and is copied
-// untransposed by cp.async, 64 positions per chunk, into tiles padded to 260
-// words: lane (tile, pair) reads positions 4 tile + 2 pair + {0, 1} of one
-// component with one 8-byte load, and a half-warp covers all 32 banks once.
-// V chunks (row-major, 64 positions) reuse the two buffers.  Every lane keeps
-// two independent f64 chains (two positions in QK, components 2 lane and
-// 2 lane + 1 in PV, one 8-byte load per position).  Scores live in shared memory, so this path serves contexts up to
+// Two launches, both 224 threads = one warp per query head of a KV head, so q
+// and the probabilities are warp broadcasts and the softmax needs no block
+// barrier:
+//  * attention_scores_kernel: one CTA per (sequence, KV head, 64-position
+//    chunk), so thousands of small CTAs keep every SM busy while K streams in.
+//    K arrives in the reference's 4-position tiles ([component][4 positions],
+//    1 KB) and is copied untransposed by cp.async into tiles padded to 260
+//    words: lane (tile, pair) reads positions 4 tile + 2 pair + {0, 1} of one
+//    component with one 8-byte load (two independent f64 chains per lane), and
+//    a half-warp covers all 32 banks once.  Scores go to the global score
+//    scratch (L2-resident).  With the RoPE table given, every CTA rotates q for
+//    its 7 heads and the CTA of the last chunk also rotates k and writes this
+//    step's K and V (decode steps, where no two rows share a slot).
+//  * attention_pv_kernel: one CTA per (sequence, KV head); the softmax of each
+//    head runs in its warp from the global scores, then V streams through two
+//    64-row buffers while every lane keeps two f64 chains (components 2 lane
+//    and 2 lane + 1, one 8-byte load per position, positions in order).
+// The probabilities live in shared memory, so this path serves contexts up to
 // kAttnMaxPositions; longer ones use the per-head kernel.
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
@@ -41,43 +50,33 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 __device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-struct AttnSmem {
-  static constexpr int kQ = kHeadsPerKv * 64;                 // q rows
-  static constexpr int kKBuf = (kChunk / 4) * kTilePitch;      // 16 padded K tiles
-  static constexpr int kVBuf = kChunk * 64;                    // V rows
-  static constexpr int kBuf = kKBuf > kVBuf ? kKBuf : kVBuf;
-  static size_t bytes(int span_cap) {
-    return (size_t)(kQ + 2 * kBuf + kHeadsPerKv * span_cap) * 4;
-  }
+struct PvSmem {
+  static constexpr int kVBuf = kChunk * 64;  // V rows
+  static size_t bytes(int span_cap) { return (size_t)(2 * kVBuf + kHeadsPerKv * span_cap) * 4; }
 };
 
-__global__ void __launch_bounds__(kThreads, 4)
-attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize, const float* rope) {
+__global__ void __launch_bounds__(kThreads, 6)
+attention_scores_kernel(Batch b, int layer, const float* rope) {
   pdl_begin();
-  extern __shared__ __align__(16) float sm[];
-  float* qs = sm;
-  float* bufs[2] = {sm + AttnSmem::kQ, sm + AttnSmem::kQ + AttnSmem::kBuf};
-  float* sc = sm + AttnSmem::kQ + 2 * AttnSmem::kBuf;  // [7][span_cap]
+  __shared__ __align__(16) float qs[kHeadsPerKv * 64];
+  __shared__ __align__(16) float ks[(kChunk / 4) * kTilePitch];
 
-  const int row = blockIdx.x >> 1, kh = blockIdx.x & 1;
+  const int t = blockIdx.x, row = blockIdx.y >> 1, kh = blockIdx.y & 1;
   const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
   const int positions = b.positions[row] + 1;
-  const int span = max((positions + 3) & ~3, b.span_min);
+  if (t * kChunk >= positions) return;
+  const bool last = (t + 1) * kChunk >= positions;
   const size_t cap = b.capacity;
   const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
   const float* kbase = kv + (size_t)layer * 4 * cap * 64 + (size_t)kh * (cap / 4) * 256;
-  const float* vbase = kv + (size_t)layer * 4 * cap * 64 + 2 * cap * 64 + (size_t)kh * cap * 64;
-  const int nchunks = (positions + kChunk - 1) / kChunk;
-  const int ntiles = (positions + 3) >> 2;
-  float* score = sc + h * span_cap;
 
   const float* qg = b.q + (size_t)row * kHidden + kh * kHeadsPerKv * 64;
   if (rope) {
     // RoPE and the KV write of this step's position (fp32_sse2.rs:1413-1428,
     // inference.rs:1809-1887), for this CTA's 7 query heads and its KV head:
-    // lane `pair` of warp h rotates (pair, pair + 32) of head 7 kh + h; warp 0
-    // also rotates K head kh and writes it, warps 0-1 write V head kh.  Only
-    // valid when no other row of the launch shares the slot (decode steps).
+    // lane `pair` of warp h rotates (pair, pair + 32) of head 7 kh + h; in the
+    // last chunk's CTA warp 0 also rotates K head kh and writes it, warps 1-2
+    // write V head kh, and the stage checks are recorded once.
     const int position = positions - 1;
     const uint32_t ord = (uint32_t)layer + 1;
     const float* table = rope + (size_t)position * 64;
@@ -88,75 +87,90 @@ attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize, const
       const float r2 = __fadd_rn(__fmul_rn(left, sn), __fmul_rn(right, c));
       qs[h * 64 + lane] = l2;
       qs[h * 64 + lane + 32] = r2;
-      const int qi = (kh * kHeadsPerKv + h) * 64 + lane;
-      check_finite(l2, &b.err[row], ord, D_ROPE, 0, qi);
-      check_finite(r2, &b.err[row], ord, D_ROPE, 0, qi + 32);
+      if (last) {
+        const int qi = (kh * kHeadsPerKv + h) * 64 + lane;
+        check_finite(l2, &b.err[row], ord, D_ROPE, 0, qi);
+        check_finite(r2, &b.err[row], ord, D_ROPE, 0, qi + 32);
+      }
     }
-    float* kvs = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
-    if (h == 0) {
-      const float* kg = b.k + (size_t)row * 128 + kh * 64;
-      const float left = kg[lane], right = kg[lane + 32];
-      const float l2 = __fsub_rn(__fmul_rn(left, c), __fmul_rn(right, sn));
-      const float r2 = __fadd_rn(__fmul_rn(left, sn), __fmul_rn(right, c));
-      check_finite(l2, &b.err[row], ord, D_ROPE, 1, kh * 64 + lane);
-      check_finite(r2, &b.err[row], ord, D_ROPE, 1, kh * 64 + lane + 32);
-      check_finite(l2, &b.err[row], ord, D_KV, 0, kh * 64 + lane);
-      check_finite(r2, &b.err[row], ord, D_KV, 0, kh * 64 + lane + 32);
-      kvs[kv_key_word(cap, layer, kh, position, lane)] = l2;
-      kvs[kv_key_word(cap, layer, kh, position, lane + 32)] = r2;
-    } else if (h <= 2) {
-      const int cc = (h - 1) * 32 + lane;
-      kvs[kv_value_word(cap, layer, kh, position, cc)] = b.v[(size_t)row * 128 + kh * 64 + cc];
+    if (last) {
+      float* kvs = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
+      if (h == 0) {
+        const float* kg = b.k + (size_t)row * 128 + kh * 64;
+        const float left = kg[lane], right = kg[lane + 32];
+        const float l2 = __fsub_rn(__fmul_rn(left, c), __fmul_rn(right, sn));
+        const float r2 = __fadd_rn(__fmul_rn(left, sn), __fmul_rn(right, c));
+        check_finite(l2, &b.err[row], ord, D_ROPE, 1, kh * 64 + lane);
+        check_finite(r2, &b.err[row], ord, D_ROPE, 1, kh * 64 + lane + 32);
+        check_finite(l2, &b.err[row], ord, D_KV, 0, kh * 64 + lane);
+        check_finite(r2, &b.err[row], ord, D_KV, 0, kh * 64 + lane + 32);
+        kvs[kv_key_word(cap, layer, kh, position, lane)] = l2;
+        kvs[kv_key_word(cap, layer, kh, position, lane + 32)] = r2;
+      } else if (h <= 2) {
+        const int cc = (h - 1) * 32 + lane;
+        kvs[kv_value_word(cap, layer, kh, position, cc)] = b.v[(size_t)row * 128 + kh * 64 + cc];
+      }
+      __threadfence();  // the cp.async reads below go through L2
     }
-    __threadfence();  // the cp.async reads below go through L2
-    __syncthreads();
   } else {
     qs[tid] = qg[tid];
     qs[tid + kThreads] = qg[tid + kThreads];
   }
+  __syncthreads();
 
   // Chunk t = K tiles 16t .. 16t + 15, each 1 KB contiguous in the cache.
-  auto load_k = [&](int t, float* dst) {
+  {
+    const int ntiles = (positions + 3) >> 2;
     const int tiles = min(kChunk / 4, ntiles - t * (kChunk / 4));
     const float* src = kbase + (size_t)t * (kChunk / 4) * 256;
     for (int i = tid; i < tiles * 64; i += kThreads)
-      cp_async16(dst + (i >> 6) * kTilePitch + (i & 63) * 4, src + i * 4);
+      cp_async16(ks + (i >> 6) * kTilePitch + (i & 63) * 4, src + i * 4);
     cp_commit();
-  };
-  load_k(0, bufs[0]);
-  if (nchunks > 1) load_k(1, bufs[1]);
-  else cp_commit();
+    cp_wait0();
+  }
+  __syncthreads();
 
-  // ---- scores: lane (tile, pair) -> positions 4 tile + 2 pair + {0, 1}
+  // lane (tile, pair) -> positions 4 tile + 2 pair + {0, 1} of the chunk
   const int tile = lane >> 1, pair = lane & 1;
   const float* qh = qs + h * 64;
-  for (int t = 0; t < nchunks; ++t) {
-    cp_wait1();
-    __syncthreads();
-    const float* kt = bufs[t & 1] + tile * kTilePitch + 2 * pair;
-    const int p = t * kChunk + 4 * tile + 2 * pair;
-    if (p < positions) {
-      double d0 = 0.0, d1 = 0.0;
+  const float* kt = ks + tile * kTilePitch + 2 * pair;
+  const int p = t * kChunk + 4 * tile + 2 * pair;
+  if (p < positions) {
+    double d0 = 0.0, d1 = 0.0;
 #pragma unroll 4
-      for (int c = 0; c < 64; c += 4) {
-        const float4 q4 = *reinterpret_cast<const float4*>(qh + c);
-        const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+    for (int c = 0; c < 64; c += 4) {
+      const float4 q4 = *reinterpret_cast<const float4*>(qh + c);
+      const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 k2 = *reinterpret_cast<const float2*>(kt + (c + j) * 4);
-          d0 += (double)__fmul_rn(qv[j], k2.x);
-          d1 += (double)__fmul_rn(qv[j], k2.y);
-        }
+      for (int j = 0; j < 4; ++j) {
+        const float2 k2 = *reinterpret_cast<const float2*>(kt + (c + j) * 4);
+        d0 += (double)__fmul_rn(qv[j], k2.x);
+        d1 += (double)__fmul_rn(qv[j], k2.y);
       }
-      score[p] = __fmul_rn((float)d0, 0.125f);
-      if (p + 1 < positions) score[p + 1] = __fmul_rn((float)d1, 0.125f);
     }
-    __syncthreads();
-    if (t + 2 < nchunks) load_k(t + 2, bufs[t & 1]);
-    else cp_commit();
+    float* out = b.scores + ((size_t)row * kQHeads + kh * kHeadsPerKv + h) * b.score_stride;
+    out[p] = __fmul_rn((float)d0, 0.125f);
+    if (p + 1 < positions) out[p + 1] = __fmul_rn((float)d1, 0.125f);
   }
-  cp_wait0();
-  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThreads, 4)
+attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
+  pdl_begin();
+  extern __shared__ __align__(16) float sm[];
+  float* bufs[2] = {sm, sm + PvSmem::kVBuf};
+  float* sc = sm + 2 * PvSmem::kVBuf;  // [7][span_cap]
+
+  const int row = blockIdx.x >> 1, kh = blockIdx.x & 1;
+  const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
+  const int positions = b.positions[row] + 1;
+  const int span = max((positions + 3) & ~3, b.span_min);
+  const size_t cap = b.capacity;
+  const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
+  const float* vbase = kv + (size_t)layer * 4 * cap * 64 + 2 * cap * 64 + (size_t)kh * cap * 64;
+  const int nchunks = (positions + kChunk - 1) / kChunk;
+  float* score = sc + h * span_cap;
+  const float* gs = b.scores + ((size_t)row * kQHeads + kh * kHeadsPerKv + h) * b.score_stride;
 
   // ---- V chunks start streaming while the softmax runs
   auto load_v = [&](int t, float* dst) {
@@ -169,12 +183,12 @@ attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize, const
   if (nchunks > 1) load_v(1, bufs[1]);
   else cp_commit();
 
-  // ---- softmax of head h, entirely within warp h
+  // ---- softmax of head h, entirely within warp h, from the global scores
   float m = fbits(0xff800000u);
-  for (int p = lane; p < positions; p += 32) m = fmaxf(m, score[p]);
+  for (int p = lane; p < positions; p += 32) m = fmaxf(m, gs[p]);
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   for (int p = lane; p < span; p += 32)
-    score[p] = p < positions ? expf4_lane(__fsub_rn(score[p], m)) : 0.0f;
+    score[p] = p < positions ? expf4_lane(__fsub_rn(gs[p], m)) : 0.0f;
   __syncwarp();
   float normalizer = 0.0f;
   if (lane == 0) {
@@ -247,17 +261,19 @@ attention_kv_group_kernel(Batch b, int layer, int span_cap, bool quantize, const
 
 int attention_smem_positions() { return kAttnMaxPositions; }
 
-void launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
-                              cudaStream_t s) {
-  const size_t bytes = AttnSmem::bytes(span_cap);
+int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
+                             cudaStream_t s) {
+  const size_t bytes = PvSmem::bytes(span_cap);
   static size_t configured = 0;  // one device per process
   if (bytes > configured) {
-    cudaFuncSetAttribute(attention_kv_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)AttnSmem::bytes(kAttnMaxPositions));
-    configured = AttnSmem::bytes(kAttnMaxPositions);
+    cudaFuncSetAttribute(attention_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)PvSmem::bytes(kAttnMaxPositions));
+    configured = PvSmem::bytes(kAttnMaxPositions);
   }
-  launch_pdl(attention_kv_group_kernel, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize,
-             rope);
+  const int chunks = (span_cap + kChunk - 1) / kChunk;
+  launch_pdl(attention_scores_kernel, dim3(chunks, b.rows * 2), kThreads, 0, s, b, layer, rope);
+  launch_pdl(attention_pv_kernel, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
+  return 2;
 }
 
 }  // namespace pb

@@ -211,6 +211,13 @@ struct pb_engine {
     prof_mark(cls);          \
     ++launches;              \
   } while (0)
+// For a launcher that returns how many kernels it launched.
+#define PB_LAUNCH_N(cls, call) \
+  do {                         \
+    prof_mark(cls);            \
+    launches += (call);        \
+    prof_mark(cls);            \
+  } while (0)
 
   pb::Batch batch(uint32_t rows, unsigned long long* err) const {
     pb::Batch b;
@@ -275,10 +282,10 @@ struct pb_engine {
       matvec(W_Q4_0, b, 896, m->tc + m->tc_qkv[layer],
              {{T(19), 896, eq}, {T(16), 128, ek}, {T(21), 128, ev}}, PB_KC_GEMV);
       if (distinct_slots) {
-        PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, max_span, true, m->rope, stream));
+        PB_LAUNCH_N(PB_KC_ATTENTION, launch_attention(b, layer, max_span, true, m->rope, stream));
       } else {
         PB_LAUNCH(PB_KC_ROPE_KV, launch_rope_kv(b, layer, m->rope, stream));
-        PB_LAUNCH(PB_KC_ATTENTION, launch_attention(b, layer, max_span, true, nullptr, stream));
+        PB_LAUNCH_N(PB_KC_ATTENTION, launch_attention(b, layer, max_span, true, nullptr, stream));
       }
       const Epilogue eo{EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_ATTN_OUTPUT};
       matvec(W_Q4_0, b, 896, m->tc + m->tc_o[layer], {{T(17), 896, eo}}, PB_KC_GEMV);

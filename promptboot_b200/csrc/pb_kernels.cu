@@ -418,15 +418,14 @@ __global__ void attention_kernel(Batch b, int layer) {
   }
 }
 
-void launch_attention(const Batch& b, int layer, int max_span, bool quantize, const float* rope,
-                      cudaStream_t s) {
-  if (max_span <= kAttnMaxPositions) {
-    launch_attention_grouped(b, layer, (max_span + 3) & ~3, quantize, rope, s);
-    return;
-  }
+int launch_attention(const Batch& b, int layer, int max_span, bool quantize, const float* rope,
+                     cudaStream_t s) {
+  if (max_span <= kAttnMaxPositions)
+    return launch_attention_grouped(b, layer, (max_span + 3) & ~3, quantize, rope, s);
   if (rope) launch_rope_kv(b, layer, rope, s);
   launch_pdl(attention_kernel, b.rows * kQHeads, 256, 0, s, b, layer);
   if (quantize) launch_quant(b, b.attn, kHidden, kHidden, s);
+  return 1 + (rope ? 1 : 0) + (quantize ? 1 : 0);
 }
 
 // -------------------------------------------------------------- argmax/top8

@@ -134,10 +134,11 @@ void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s
 // rope (optional): apply RoPE to q/k and write this step's K/V first (what
 // launch_rope_kv does), fused into the attention launch; only when every row
 // of the batch has its own slot.
-void launch_attention(const Batch& b, int layer, int max_span, bool quantize, const float* rope,
-                      cudaStream_t s);
-void launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
-                              cudaStream_t s);
+// Both return the number of kernels they launched.
+int launch_attention(const Batch& b, int layer, int max_span, bool quantize, const float* rope,
+                     cudaStream_t s);
+int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
+                             cudaStream_t s);
 void launch_swiglu_quant(const Batch& b, uint32_t layer_ordinal, cudaStream_t s);
 void launch_argmax(const float* logits, size_t ld, int rows, int words, uint32_t* ids,
                    uint32_t* bits, unsigned long long* first_nonfinite, cudaStream_t s);

@@ -460,15 +460,15 @@ uint32_t pb_attention_device(const float* q, const float* kv, uint32_t capacity,
   OpScratch scr(s);
   PB_CUDA(scr.alloc(rows));
   PB_CUDA(cudaMemcpyAsync(scr.positions, positions_host, rows * 4, cudaMemcpyHostToDevice, s));
-  float* sc = scores;
-  if (!sc) PB_CUDA(cudaMallocAsync(&sc, (size_t)rows * 14 * span_max * 4, s));
+  float* sc = nullptr;  // raw scores; the probabilities go to `scores`
+  PB_CUDA(cudaMallocAsync(&sc, (size_t)rows * 14 * span_max * 4, s));
   pb::Batch b = scr.batch(rows);
   b.q = const_cast<float*>(q); b.kv = const_cast<float*>(kv); b.capacity = capacity;
   b.attn = out; b.scores = sc; b.score_stride = span_max; b.span_min = (int)span;
   b.probs_out = scores;
   pb::launch_attention(b, (int)layer, (int)span_max, false, nullptr, s);
   PB_CUDA(cudaGetLastError());
-  if (!scores) PB_CUDA(cudaFreeAsync(sc, s));
+  PB_CUDA(cudaFreeAsync(sc, s));
   return PB_OK;
 }
 

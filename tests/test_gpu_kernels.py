@@ -181,6 +181,68 @@ def test_attention_random_kv_matches_oracle(positions, cap):
         assert np.array_equal(u32(got[r]), u32(ref)), (r, positions[r])
 
 
+def _same_bits_or_nan(got, ref):
+    """Bit equality, except that a NaN only has to be a NaN (its payload is the
+    device's, not the host's)."""
+    g, r = u32(got), u32(ref)
+    nan = np.isnan(ref)
+    return np.array_equal(np.isnan(got), nan) and np.array_equal(g[~nan], r[~nan])
+
+
+@pytest.mark.parametrize("case", ["overflowing_products", "overflowing_scores", "huge_but_finite",
+                                  "inf_value", "nan_query", "nan_key", "tiny_products"])
+def test_attention_extreme_magnitudes_match_oracle(case):
+    """Non-finite and extreme values through the grouped kernel against the
+    oracle: products that overflow binary32, finite products whose f64 sum
+    overflows the binary32 score, huge but finite products, infinite V, NaN
+    queries and keys, and products in the binary32 subnormal range."""
+    lib = _lib.load()
+    cap, layer = 256, 2
+    positions = [0, 69, 130, 191]
+    rows = len(positions)
+    rng = np.random.default_rng(sum(map(ord, case)))
+    kv = np.zeros(rows * 24 * 4 * cap * 64, dtype=np.float32)
+    q = rng.standard_normal((rows, 896)).astype(np.float32)
+    for r in range(rows):
+        base = r * 24 * 4 * cap * 64 + layer * 4 * cap * 64
+        kv[base:base + 4 * cap * 64] = rng.standard_normal(4 * cap * 64).astype(np.float32)
+        kvr = kv[base:base + 4 * cap * 64]
+        p = positions[r] // 2
+        if case == "overflowing_products":      # |q k| > FLT_MAX in head 7
+            q[r, 70:80] *= np.float32(3e19)
+            q[r, 7 * 64 + 5] = np.float32(3e19)
+            kvr[oracle.kv_word(cap, 0, 0, p, 1, 5)] = np.float32(2e20)
+            kvr[oracle.kv_word(cap, 0, 0, p, 1, 9)] = np.float32(-2e20)
+        elif case == "overflowing_scores":      # finite products, sum beyond FLT_MAX
+            q[r, :64] = np.float32(1.2e19)
+            for c in range(64):
+                kvr[oracle.kv_word(cap, 0, 0, p, 0, c)] = np.float32(1.2e19)
+        elif case == "huge_but_finite":         # max|q| max|k| >= 2^127, no product overflows
+            q[r, 448] = np.float32(1e30)
+            kvr[oracle.kv_word(cap, 0, 0, p, 1, 3)] = np.float32(1e10)
+        elif case == "inf_value":
+            kvr[oracle.kv_word(cap, 0, 1, p, 0, 17)] = np.float32(np.inf)
+            kvr[oracle.kv_word(cap, 0, 1, positions[r], 1, 40)] = np.float32(-np.inf)
+        elif case == "nan_query":
+            q[r, 3 + 64 * r] = np.float32(np.nan)
+        elif case == "nan_key":
+            kvr[oracle.kv_word(cap, 0, 0, positions[r], 0, 63)] = np.float32(np.nan)
+        else:                                   # products in the f32 subnormal range
+            q[r] *= np.float32(2.0 ** -70)
+            kvr[:2 * cap * 64] *= np.float32(2.0 ** -70)
+    out = torch.zeros((rows, 896), dtype=torch.float32, device="cuda")
+    pos = np.array(positions, dtype=np.uint32)
+    assert lib.pb_attention_device(ptr(dev(q)), ptr(dev(kv)), cap, layer,
+                                   pos.ctypes.data_as(ctypes.c_void_p), rows, 0, ptr(out), None,
+                                   None) == 0
+    sync()
+    got = host(out)
+    for r in range(rows):
+        kvr = kv[r * 24 * 4 * cap * 64:(r + 1) * 24 * 4 * cap * 64]
+        ref, _ = oracle.attention(q[r], kvr, cap, layer, positions[r], (positions[r] + 4) & ~3)
+        assert _same_bits_or_nan(got[r], ref), (case, r, positions[r])
+
+
 def _q4_weights(rng, rows, cols):
     nb = rows * cols // 32
     scales = (np.abs(rng.standard_normal(nb) * 0.02) / 8).astype(np.float16)
