@@ -350,8 +350,9 @@ def profiled_traffic(kernel_class: str, seqs: int, mean_ctx: float):
 
 # What bounds each kernel class in practice (ncu captures under profiles/).
 LIMITERS = {
-    "attention": "f32->f64 widening of every product on the XU pipe (57% busy in "
-                 "profiles/attention_kv_group_r192_p520.md); HBM traffic is 1031 B per "
+    "attention": "f32->f64 widening of every product on the XU pipe (85% busy in the "
+                 "scores launch, 61% in the latency-bound softmax+PV launch, "
+                 "profiles/attention_scores_pv_r256_p520.md); HBM traffic is 1087 B per "
                  "sequence-position, the algorithmic 1024 B",
     "gemv": "per-block binary32 epilogue on the FMA pipe and bulk-copy issue "
             "(profiles/qgemm_tc_*.md)",
