@@ -50,6 +50,28 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 __device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+// f64 bits of fl(a * b) * 2^-896, for a finite product: the sign stays in bit
+// 31 of the high word, exponent and fraction move down three bits (the
+// arithmetic shift's copies of the sign in bits 30..28 are cleared) and the
+// fraction's low three bits open the low word; f32 subnormals land on f64
+// subnormals with the same scale.  A chain that adds these images instead of
+// f64(fl(a * b)) and multiplies by 2^896 at the end rounds exactly as the
+// reference's chain: every term is a multiple of 2^-1045 once scaled, so a
+// partial sum below the f64 normal range is exact in both domains, above it
+// the roundings coincide, and no partial sum comes near either end of the
+// range.  Three integer operations instead of one conversion on the XU pipe.
+__device__ __forceinline__ double scaled_product(float a, float b) {
+  double d;
+  asm("{\n\t.reg .b32 t, hi, lo;\n\t"
+      "mul.rn.f32 t, %1, %2;\n\t"
+      "shr.s32 hi, t, 3;\n\t"
+      "and.b32 hi, hi, 0x8FFFFFFF;\n\t"
+      "shl.b32 lo, t, 29;\n\t"
+      "mov.b64 %0, {lo, hi};\n\t}"
+      : "=d"(d) : "f"(a), "f"(b));
+  return d;
+}
+
 struct PvSmem {
   static constexpr int kVBuf = kChunk * 64;  // V rows
   static size_t bytes(int span_cap) { return (size_t)(2 * kVBuf + kHeadsPerKv * span_cap) * 4; }
@@ -154,6 +176,7 @@ attention_scores_kernel(Batch b, int layer, const float* rope) {
   }
 }
 
+template <bool kCheckV>
 __global__ void __launch_bounds__(kThreads, 4)
 attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
   pdl_begin();
@@ -208,8 +231,14 @@ attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
   }
 
   // ---- values: lane owns components 2 lane and 2 lane + 1 of head h (one
-  // 8-byte load per position), positions in order
+  // 8-byte load per position), positions in order.  Component 2 lane + 1 sums
+  // scaled images (scaled_product), valid when every product is finite: the
+  // probabilities are (a finite normalizer means every e was finite), and
+  // V is: checked at its write (Batch::kv_checked), or here, where
+  // fma(v, 0, vchk) stays zero while every V word of the chain is finite;
+  // otherwise the lane redoes that chain with conversions below.
   double acc0 = 0.0, acc1 = 0.0;
+  float vchk = 0.0f;
   for (int t = 0; t < nchunks; ++t) {
     cp_wait1();
     __syncthreads();
@@ -224,19 +253,28 @@ attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
       for (int j = 0; j < 4; ++j) {
         const float2 v2 = *reinterpret_cast<const float2*>(vt + (i + j) * 64);
         acc0 += (double)__fmul_rn(pv[j], v2.x);
-        acc1 += (double)__fmul_rn(pv[j], v2.y);
+        acc1 += scaled_product(pv[j], v2.y);
+        if (kCheckV) vchk = __fmaf_rn(v2.y, 0.0f, vchk);
       }
     }
     for (; i < rows_here; ++i) {
       const float2 v2 = *reinterpret_cast<const float2*>(vt + i * 64);
       acc0 += (double)__fmul_rn(pr[i], v2.x);
-      acc1 += (double)__fmul_rn(pr[i], v2.y);
+      acc1 += scaled_product(pr[i], v2.y);
+      if (kCheckV) vchk = __fmaf_rn(v2.y, 0.0f, vchk);
     }
     __syncthreads();
     if (t + 2 < nchunks) load_v(t + 2, bufs[t & 1]);
     else cp_commit();
   }
   cp_wait0();
+  if (fabsf(normalizer) <= 0x1.fffffep127f && vchk == 0.0f) {
+    acc1 *= 0x1p896;
+  } else {
+    acc1 = 0.0;
+    for (int p = 0; p < positions; ++p)
+      acc1 += (double)__fmul_rn(score[p], vbase[(size_t)p * 64 + 2 * lane + 1]);
+  }
   const float o0 = (float)acc0, o1 = (float)acc1;
   const int qh_index = kh * kHeadsPerKv + h;
   float* out = b.attn + (size_t)row * kHidden + qh_index * 64;
@@ -266,13 +304,18 @@ int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quant
   const size_t bytes = PvSmem::bytes(span_cap);
   static size_t configured = 0;  // one device per process
   if (bytes > configured) {
-    cudaFuncSetAttribute(attention_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(attention_pv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)PvSmem::bytes(kAttnMaxPositions));
+    cudaFuncSetAttribute(attention_pv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)PvSmem::bytes(kAttnMaxPositions));
     configured = PvSmem::bytes(kAttnMaxPositions);
   }
   const int chunks = (span_cap + kChunk - 1) / kChunk;
   launch_pdl(attention_scores_kernel, dim3(chunks, b.rows * 2), kThreads, 0, s, b, layer, rope);
-  launch_pdl(attention_pv_kernel, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
+  if (b.kv_checked)
+    launch_pdl(attention_pv_kernel<false>, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
+  else
+    launch_pdl(attention_pv_kernel<true>, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
   return 2;
 }
 

@@ -226,6 +226,7 @@ struct pb_engine {
     b.attn = attn; b.gate = gate; b.up = up; b.logits = logits; b.scores = scores;
     b.score_stride = capacity + 4; b.kv = kv; b.capacity = capacity; b.history = history;
     b.err = err;
+    b.kv_checked = true;
     if ((int)rows >= pb::kTcMinBatch) {
       b.aq_tc = aq_tc; b.tc_seqs = tc_seqs;
     }

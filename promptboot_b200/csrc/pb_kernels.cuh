@@ -56,6 +56,11 @@ struct Batch {
   float* product_out = nullptr;  // optional [B][4864] SwiGLU output (operator API)
   int span_min = 0;              // minimum softmax span (operator API; 0 = natural)
   float* probs_out = nullptr;    // optional [B][14][score_stride] final probabilities
+  // Every V word below each row's position came from this engine's own
+  // forwards, whose v-projection stage check faults a row on a non-finite
+  // word before it is written (rows read after such a fault are discarded),
+  // so attention need not re-check V.
+  bool kv_checked = false;
   // Tensor-core activation layout, written by the quantizers when aq_tc is set
   // (instead of the row-major aq/ad/asum),
   // chunk-major (4 Q-blocks per chunk) so one chunk of one sequence tile is one

@@ -190,12 +190,15 @@ def _same_bits_or_nan(got, ref):
 
 
 @pytest.mark.parametrize("case", ["overflowing_products", "overflowing_scores", "huge_but_finite",
-                                  "inf_value", "nan_query", "nan_key", "tiny_products"])
+                                  "inf_value", "nan_query", "nan_key", "tiny_products",
+                                  "tiny_values", "wide_values"])
 def test_attention_extreme_magnitudes_match_oracle(case):
-    """Non-finite and extreme values through the grouped kernel against the
+    """Non-finite and extreme values through the grouped kernels against the
     oracle: products that overflow binary32, finite products whose f64 sum
     overflows the binary32 score, huge but finite products, infinite V, NaN
-    queries and keys, and products in the binary32 subnormal range."""
+    queries and keys, products in the binary32 subnormal range, and V spread
+    over 170 binades (the PV chain summed as scaled f64 images, and its exact
+    fallback when a probability or a V word is not finite)."""
     lib = _lib.load()
     cap, layer = 256, 2
     positions = [0, 69, 130, 191]
@@ -227,9 +230,14 @@ def test_attention_extreme_magnitudes_match_oracle(case):
             q[r, 3 + 64 * r] = np.float32(np.nan)
         elif case == "nan_key":
             kvr[oracle.kv_word(cap, 0, 0, positions[r], 0, 63)] = np.float32(np.nan)
-        else:                                   # products in the f32 subnormal range
+        elif case == "tiny_products":           # q.k products in the f32 subnormal range
             q[r] *= np.float32(2.0 ** -70)
             kvr[:2 * cap * 64] *= np.float32(2.0 ** -70)
+        elif case == "tiny_values":             # p.v products subnormal or zero
+            kvr[2 * cap * 64:] *= np.float32(2.0 ** -128)
+        else:                                   # V over 170 binades: rounding in every f64 sum
+            e = rng.integers(-140, 31, 2 * cap * 64)
+            kvr[2 * cap * 64:] = (kvr[2 * cap * 64:] * np.exp2(e)).astype(np.float32)
     out = torch.zeros((rows, 896), dtype=torch.float32, device="cuda")
     pos = np.array(positions, dtype=np.uint32)
     assert lib.pb_attention_device(ptr(dev(q)), ptr(dev(kv)), cap, layer,
