@@ -16,10 +16,10 @@
 // one transaction-count mbarrier, issued by one thread.
 //
 // One tcgen05.mma per Q-block: M = 128 weight rows, N = NT sequences, K = 32,
-// both operands signed.  TMEM columns are preloaded with 0x4B400000 and the MMA
-// accumulates into them, so each column reads back as the binary32 bit pattern
-// of 1.5 * 2^23 + i (exact for |i| < 2^22; |i| <= 2^19 here); the epilogue
-// writes the constant back after reading.  Epilogue per (row, sequence, block),
+// both operands signed, without accumulation: each block's int32 dot i lands on
+// its own TMEM columns, and the epilogue adds 0x4B400000 to the word as an
+// integer, giving the binary32 bit pattern of 1.5 * 2^23 + i (exact for
+// |i| < 2^22; |i| <= 2^19 here).  Epilogue per (row, sequence, block),
 // on packed f32x2 operations (two sequences per instruction, IEEE RN per lane;
 // the assembler fuses a packed multiply into a following packed add even with
 // explicit rounding, so each rounded product is an fma with a run-time -0.0
@@ -98,15 +98,15 @@ __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
-// D[tmem] += A * B (accumulates into the preloaded columns).
-__device__ __forceinline__ void mma_i8_acc(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                           uint32_t idesc) {
-  const uint32_t one = 1, zero = 0;
+// D[tmem] = A * B (enable-input-d false: each block's dot lands on its own
+// columns, no accumulation).
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  const uint32_t zero = 0;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(one), "r"(zero)
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%4, %4, %4, %4}, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(zero)
       : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -123,19 +123,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "r"(taddr)
       : "memory");
 }
-// Writes one 32-bit value to 16 consecutive columns of the warp's 32 lanes.
-__device__ __forceinline__ void tmem_st16_same(uint32_t taddr, uint32_t x) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(
-          taddr),
-      "r"(x)
-      : "memory");
-}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // K-major, no swizzle: leading byte offset (between the two 16-byte K halves)
@@ -288,24 +277,6 @@ __device__ __forceinline__ void tmem_ld_cols<4>(uint32_t taddr, uint32_t (&v)[4]
                : "r"(taddr)
                : "memory");
 }
-template <int N>
-__device__ __forceinline__ void tmem_st_same(uint32_t taddr, uint32_t x);
-template <>
-__device__ __forceinline__ void tmem_st_same<4>(uint32_t taddr, uint32_t x) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%1,%1,%1};" ::"r"(taddr), "r"(x)
-               : "memory");
-}
-template <>
-__device__ __forceinline__ void tmem_st_same<16>(uint32_t taddr, uint32_t x) {
-  tmem_st16_same(taddr, x);
-}
-template <>
-__device__ __forceinline__ void tmem_st_same<8>(uint32_t taddr, uint32_t x) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-               "r"(x)
-               : "memory");
-}
-
 // Persistent: CTA i serves tiles i, i + G, i + 2G, ... (G = gridDim.x) of the
 // (row tile, sequence tile) grid, sequence tile fastest, so CTAs running at the
 // same time share weight tiles in L2; the ring, the MMA issue and the TMEM
@@ -360,11 +331,6 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
   tc_after_sync();
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t tlane = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(cg * CPW);
-  if (warp >= 2) {
-#pragma unroll
-    for (int k = 0; k < G * kKC; ++k) tmem_st_same<CPW>(tlane + (uint32_t)(k * NT), kMagic);
-    tmem_wait_st();
-  }
   tc_before_sync();
   __syncthreads();
   tc_after_sync();
@@ -427,8 +393,8 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
           const uint8_t* sp = smem + st * C::kStage;
 #pragma unroll
           for (int j = 0; j < kKC; ++j)
-            mma_i8_acc(tmem_base + (uint32_t)((gr * kKC + j) * NT), smem_desc(sp + j * kATile, 256),
-                       smem_desc(sp + C::kBOff + j * 256, kTcGroupBytes), kIdesc);
+            mma_i8(tmem_base + (uint32_t)((gr * kKC + j) * NT), smem_desc(sp + j * kATile, 256),
+                   smem_desc(sp + C::kBOff + j * 256, kTcGroupBytes), kIdesc);
           mma_commit(&tfull[gr]);
           mma_last = q;
         }
@@ -469,8 +435,6 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
 #pragma unroll
           for (int jj = 0; jj < BT; ++jj) tmem_ld_cols<CPW>(tg + (uint32_t)((jb + jj) * NT), v[jj]);
           tmem_wait_ld();
-#pragma unroll
-          for (int jj = 0; jj < BT; ++jj) tmem_st_same<CPW>(tg + (uint32_t)((jb + jj) * NT), kMagic);
           uint64_t w2[BT], n2[BT];
           bool exact_fma = true;  // Q4_0: fma(x, dW, -1.5*2^23*dW) needs a finite dW
 #pragma unroll
@@ -491,7 +455,8 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
                 const int s = s0 + 2 * p;
                 const uint64_t da2 = *reinterpret_cast<const uint64_t*>(
                     sp + C::kBOff + (s >> 3) * kTcGroupBytes + 1024 + ((jb + jj) * 8 + (s & 7)) * 4);
-                const uint64_t x2 = pk_u(v[jj][2 * p], v[jj][2 * p + 1]);
+                // bits of 1.5 * 2^23 + i, exactly, for the block dot i (|i| < 2^22)
+                const uint64_t x2 = pk_u(v[jj][2 * p] + kMagic, v[jj][2 * p + 1] + kMagic);
                 uint64_t t;
                 if (Q4) {
                   // Non-finite dW (never in a sane image): fl(f32(i) * dW) with
@@ -510,7 +475,6 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
           if (!Q4 || exact_fma) accumulate(std::true_type{});
           else accumulate(std::false_type{});
         }
-        tmem_wait_st();
         tc_before_sync();
         __syncwarp();
         if (lane == 0) {
