@@ -87,22 +87,31 @@ __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t*
   // Float image of the list's K-th key: a penalty only lowers a value (x/1.1
   // for x >= 0, 1.1x for x < 0, zeros unchanged), so a raw value below it can
   // never enter the list and skips the key work; equal values go on to the
-  // exact (value, id) key comparison.  Non-finite values always go on (they are
-  // recorded as the row's first non-finite word).
+  // exact (value, id) key comparison.  One compare per value and one warp vote
+  // per four values; non-finite values are not ranked here but leave
+  // fma(v, 0, fin) NaN, and the row is then rescanned for its first one.
   float thr_f = fbits(0xff800000u);
+  float fin = 0.0f;
   auto offer = [&](float val, int i) {
-    const uint32_t vb = bitsf(val);
-    const bool nonfinite = !finite_bits(vb);
-    const bool cand = i < end && (val >= thr_f || nonfinite);
-    if (__ballot_sync(kFull, cand) == 0) return;
     unsigned long long key = 0;
-    if (cand) {
-      if (nonfinite) atomicMin(bad, ((unsigned long long)i << 32) | vb);
+    if (i < end && val >= thr_f) {
       if (penal && (penal[i >> 5] >> (i & 31) & 1u)) val = penalize(val);
       key = make_key(val, (uint32_t)i);
     }
     list_offer<K>(entry, thr, key, lane);
     thr_f = thr == 0 ? fbits(0xff800000u) : key_value(thr);
+  };
+  auto offer4 = [&](float v0, float v1, float v2, float v3, int i0) {
+    fin = __fmaf_rn(v0, 0.0f, fin);
+    fin = __fmaf_rn(v1, 0.0f, fin);
+    fin = __fmaf_rn(v2, 0.0f, fin);
+    fin = __fmaf_rn(v3, 0.0f, fin);
+    const bool any = v0 >= thr_f || v1 >= thr_f || v2 >= thr_f || v3 >= thr_f;
+    if (__ballot_sync(kFull, any) == 0) return;
+    offer(v0, i0);
+    offer(v1, i0 + 1);
+    offer(v2, i0 + 2);
+    offer(v3, i0 + 3);
   };
   // Software pipeline: the next four 512-byte loads of the warp are in flight
   // while the current four are ranked.
@@ -122,13 +131,8 @@ __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t*
           nxt[u] = *reinterpret_cast<const float4*>(x + next + u * 128 + lane * 4);
       }
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int i0 = base + u * 128 + lane * 4;
-        offer(cur[u].x, i0);
-        offer(cur[u].y, i0 + 1);
-        offer(cur[u].z, i0 + 2);
-        offer(cur[u].w, i0 + 3);
-      }
+      for (int u = 0; u < kBatch; ++u)
+        offer4(cur[u].x, cur[u].y, cur[u].z, cur[u].w, base + u * 128 + lane * 4);
       base = next;
       if (!more) break;
 #pragma unroll
@@ -145,11 +149,17 @@ __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t*
 #pragma unroll
       for (int j = 0; j < 4; ++j) v[j] = (i0 + j < end) ? x[i0 + j] : 0.0f;
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) offer(v[j], i0 + j);
+    offer4(v[0], v[1], v[2], v[3], i0);
   }
   if (lane < K) warp_keys[warp * K + lane] = entry;
-  __syncthreads();
+  if (__syncthreads_or(fin != 0.0f)) {
+    // some value is not finite: the first one, in index order
+    for (int i = threadIdx.x; i < words; i += blockDim.x) {
+      const uint32_t vb = bitsf(x[i]);
+      if (!finite_bits(vb)) atomicMin(bad, ((unsigned long long)i << 32) | vb);
+    }
+    __syncthreads();
+  }
   if (warp == 0) {
     entry = 0;
     thr = 0;

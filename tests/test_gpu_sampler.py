@@ -166,3 +166,37 @@ def test_device_batch_sampler_rejects_rows_transactionally():
     after = d_logits.cpu().numpy()
     assert np.array_equal(f32bits(after[1]), f32bits(logits[1]))
     assert np.array_equal(f32bits(after[2]), f32bits(logits[2]))
+
+
+def test_device_batch_sampler_reports_first_nonfinite_word():
+    """The first non-finite logit in index order (its bits as stored) across the
+    row's warp segments and the unaligned tail; rows without one still sample."""
+    logits, history = config1_batch(4, seed=9)
+    nan_bits = np.array([0x7FC00123], dtype=np.uint32).view(np.float32)[0]
+    logits[0, 150000] = nan_bits
+    logits[0, 70001] = -np.inf
+    logits[0, 90000] = np.inf
+    logits[1, 5] = nan_bits
+    logits[2, V - 1] = np.inf
+    lib = _lib.load()
+    d_logits = dev(logits)
+    states = np.array([[21, 0], [22, 0], [23, 0], [24, 0]], dtype=np.uint64)
+    d_states = dev(states)
+    out = torch.zeros((4, 4), dtype=torch.int32, device="cuda")
+    assert lib.pb_sample_batch_device(ptr(d_logits), V, 4, ptr(dev(history.reshape(-1))),
+                                      ptr(dev(np.arange(4, dtype=np.uint64) * 512)),
+                                      ptr(dev(np.full(4, 512, dtype=np.uint32))), ptr(d_states),
+                                      ptr(out), None) == 0
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint32)
+    st = d_states.cpu().numpy().view(np.uint64)
+    assert list(got[0, :3]) == [7, 70001, 0xFF800000] and list(st[0]) == [21, 0]
+    assert list(got[1, :3]) == [7, 5, 0x7FC00123] and list(st[1]) == [22, 0]
+    assert list(got[2, :3]) == [7, V - 1, 0x7F800000] and list(st[2]) == [23, 0]
+    assert got[3, 0] == 0 and st[3, 1] == 1
+    seen = np.zeros(api.SEEN_BYTES, dtype=np.uint8)
+    ref_logits = logits[3].copy()
+    oracle.lib().orc_apply_repetition_penalty(oracle._p(ref_logits), oracle._p(history[3]), 512,
+                                              oracle._p(seen))
+    master = oracle.SamplingState(24)
+    assert got[3, 3] == oracle.sample_top_k_top_p(ref_logits, master.next_24())
