@@ -277,9 +277,12 @@ def model_image(rank: int, world: int):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+    """nvidia-smi clocks and throttle reasons, sampled every 50 ms from before
+    the timed region (the first sample is awaited, so the sampler is running
+    when the region starts) and summarised over the samples whose timestamps
+    fall inside the region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -287,20 +290,29 @@ class ClockSampler:
         self.path = pathlib.Path(tempfile.mkstemp(prefix="pb_clocks_", suffix=".csv")[1])
         self.device = device
         self.proc = None
+        self.window = None
 
     def __enter__(self):
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.fh, stderr=subprocess.DEVNULL)
+            deadline = time.time() + 5.0
+            while time.time() < deadline and self.path.stat().st_size == 0:
+                time.sleep(0.01)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
+    def mark(self, t0: float, t1: float):
+        """Wall-clock bounds (time.time()) of the timed region."""
+        self.window = (t0, t1)
+
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.06)  # one more sample after the region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -309,16 +321,30 @@ class ClockSampler:
             self.fh.close()
 
     def summary(self):
+        import datetime
         rows = []
         try:
             for line in self.path.read_text().splitlines():
                 f = [x.strip() for x in line.split(",")]
-                if len(f) >= 9 and f[1].isdigit():
-                    rows.append(f)
+                if len(f) >= 10 and f[2].isdigit():
+                    try:
+                        ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    except ValueError:
+                        continue
+                    rows.append((ts, f[1:]))
         except OSError:
             pass
         finally:
             self.path.unlink(missing_ok=True)
+        if self.window:
+            t0, t1 = self.window
+            inside = [r for ts, r in rows if t0 <= ts <= t1]
+            if not inside:  # a region shorter than the period: the first sample after it began
+                after = [r for ts, r in rows if ts >= t0]
+                inside = after[:1]
+            rows = inside
+        else:
+            rows = [r for _, r in rows]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -435,7 +461,7 @@ def run_ours(args, world, rank, local):
     status, _, errs = eng.prefill_batch(seqs, prompts, C - P)
     if status:
         raise RuntimeError(f"prefill failed: {errs[0].tuple()}")
-    states = [api.SamplingState(shard.sampling_seed(g)) for g in gidx]
+    states = api.SamplingStates([shard.sampling_seed(g) for g in gidx])
     stream = torch.cuda.ExternalStream(lib.pb_engine_stream(eng._h))
 
     # warm-up with every kernel class timed, to name the dominant kernel
@@ -457,12 +483,14 @@ def run_ours(args, world, rank, local):
         barrier(world)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.time()
         e0.record(stream)
         torch.cuda.nvtx.range_push("pb_timed")  # ncu --nvtx --nvtx-include pb_timed/
         st, _, errs = eng.generate(seqs, states, args.steps, want_tokens=False)
         torch.cuda.nvtx.range_pop()
         e1.record(stream)
         torch.cuda.synchronize()
+        clock.mark(w0, time.time())
         barrier(world)
     if st:
         raise RuntimeError(f"timed steps failed: {[e.tuple() for e in errs if e.status][:1]}")

@@ -8,6 +8,7 @@ leave state untouched where the reference's prechecks do.
 """
 from __future__ import annotations
 
+import collections.abc
 import ctypes
 from dataclasses import dataclass
 
@@ -65,6 +66,23 @@ def _step(s: _lib.PbStep) -> InferenceStep:
     return InferenceStep(s.position, s.selected_token, s.selected_logit_bits, s.eos)
 
 
+class _Steps(collections.abc.Sequence):
+    """The InferenceStep results of a batched call, converted on access (a
+    batch of 256 converted eagerly costs more host time than a decode step's
+    launches)."""
+
+    def __init__(self, arr):
+        self._a = arr
+
+    def __len__(self):
+        return len(self._a)
+
+    def __getitem__(self, i):
+        if isinstance(i, slice):
+            return [_step(x) for x in self._a[i]]
+        return _step(self._a[i])
+
+
 def _check(status: int, err: _lib.PbError):
     if status == 0:
         return
@@ -105,6 +123,51 @@ class SamplingState:
         c = SamplingState(1)
         c._s.state, c._s.draws = self._s.state, self._s.draws
         return c
+
+
+class SamplingStates(collections.abc.Sequence):
+    """A batch of SamplingState held in one contiguous array, the layout the
+    batched entry points take: passing it to sample / generate costs no
+    per-row copies.  Item i is a SamplingState sharing row i's memory."""
+
+    def __init__(self, seeds):
+        seeds = [int(x) for x in seeds]
+        self._arr = (_lib.PbSamplingState * len(seeds))()
+        init = _lib.load().pb_sampling_state_init
+        for i, seed in enumerate(seeds):
+            init(ctypes.byref(self._arr[i]), seed & (2**64 - 1))
+
+    def __len__(self):
+        return len(self._arr)
+
+    def __getitem__(self, i):
+        if isinstance(i, slice):
+            return [self[j] for j in range(*i.indices(len(self)))]
+        if i < 0:
+            i += len(self)
+        if not 0 <= i < len(self):
+            raise IndexError(i)
+        view = SamplingState.__new__(SamplingState)
+        view._s = _lib.PbSamplingState.from_buffer(self._arr, i * ctypes.sizeof(_lib.PbSamplingState))
+        return view
+
+
+def _state_array(states, n: int):
+    if isinstance(states, SamplingStates):
+        if len(states) != n:
+            raise ValueError("one sampling state per sequence")
+        return states._arr
+    arr = (_lib.PbSamplingState * n)()
+    for i, s in enumerate(states):
+        arr[i] = s._s
+    return arr
+
+
+def _state_back(states, arr):
+    if isinstance(states, SamplingStates):
+        return
+    for i, s in enumerate(states):
+        s._s.state, s._s.draws = arr[i].state, arr[i].draws
 
 
 def sample_token(logits, state: SamplingState) -> int:
@@ -288,6 +351,8 @@ class InferenceEngine:
         return st, [_step(s) for s in steps], list(errs)
 
     def decode_batch(self, seqs, tokens, require_greedy: bool = False):
+        """One decode step of every listed sequence; returns (status, steps,
+        errors), steps and errors indexable per row."""
         seqs = _u32(seqs)
         toks = _u32(tokens)
         steps = (_lib.PbStep * seqs.size)()
@@ -296,7 +361,7 @@ class InferenceEngine:
                                                 int(require_greedy), steps, errs)
         if st == 100:
             raise DeviceError(_lib.last_error())
-        return st, [_step(s) for s in steps], list(errs)
+        return st, _Steps(steps), errs
 
     def logits(self, row: int = 0) -> np.ndarray:
         out = np.zeros(VOCAB, dtype=np.uint32)
@@ -306,32 +371,28 @@ class InferenceEngine:
         return out
 
     def sample(self, seqs, states):
-        """sample_token_with_repetition on the last step's rows, on the GPU."""
+        """sample_token_with_repetition on the last step's rows, on the GPU.
+        `states`: a SamplingStates batch (updated in place, no copies) or a
+        list of SamplingState."""
         seqs = _u32(seqs)
-        arr = (_lib.PbSamplingState * seqs.size)()
-        for i, s in enumerate(states):
-            arr[i] = s._s
+        arr = _state_array(states, seqs.size)
         ids = np.zeros(seqs.size, dtype=np.uint32)
         errs = (_lib.PbError * seqs.size)()
         st = _lib.load().pb_engine_sample(self._h, seqs.size, _ptr(seqs), arr, _ptr(ids), errs)
         if st == 100:
             raise DeviceError(_lib.last_error())
-        for i, s in enumerate(states):
-            s._s.state, s._s.draws = arr[i].state, arr[i].draws
-        return st, ids, list(errs)
+        _state_back(states, arr)
+        return st, ids, errs
 
     def generate(self, seqs, states, steps: int, want_tokens: bool = True):
         """Device-resident sample -> decode_selected loop (fixed length)."""
         seqs = _u32(seqs)
-        arr = (_lib.PbSamplingState * seqs.size)()
-        for i, s in enumerate(states):
-            arr[i] = s._s
+        arr = _state_array(states, seqs.size)
         out = np.zeros((steps, seqs.size), dtype=np.uint32) if want_tokens else None
         errs = (_lib.PbError * seqs.size)()
         st = _lib.load().pb_engine_generate(self._h, seqs.size, _ptr(seqs), arr, steps,
                                             _ptr(out), errs)
         if st == 100:
             raise DeviceError(_lib.last_error())
-        for i, s in enumerate(states):
-            s._s.state, s._s.draws = arr[i].state, arr[i].draws
+        _state_back(states, arr)
         return st, out, list(errs)

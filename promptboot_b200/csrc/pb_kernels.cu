@@ -441,13 +441,39 @@ __global__ void argmax_kernel(const float* __restrict__ logits, size_t ld, int w
   const float* x = logits + (size_t)blockIdx.x * ld;
   float best = fbits(0xff800000u);
   int besti = 0x7fffffff;
-  for (int i = threadIdx.x; i < words; i += blockDim.x) {
-    float v = x[i];
-    uint32_t vb = bitsf(v);
+  // Each thread visits its indices in increasing order, so strict > keeps the
+  // earliest of equal values; four 16-byte loads in flight per thread.
+  auto consider = [&](float v, int i) {
+    const uint32_t vb = bitsf(v);
     if (!finite_bits(vb) && first_nonfinite)
       atomicMin(&first_nonfinite[blockIdx.x], ((unsigned long long)i << 32) | vb);
     if (v > best || besti == 0x7fffffff) { best = v; besti = i; }
+  };
+  const int nvec = (ld % 4 == 0) ? words / 4 : 0;
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  const int stride = (int)blockDim.x;
+  int f = threadIdx.x;
+  for (; f + 3 * stride < nvec; f += 4 * stride) {
+    float4 a[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) a[u] = x4[f + u * stride];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i0 = 4 * (f + u * stride);
+      consider(a[u].x, i0);
+      consider(a[u].y, i0 + 1);
+      consider(a[u].z, i0 + 2);
+      consider(a[u].w, i0 + 3);
+    }
   }
+  for (; f < nvec; f += stride) {
+    const float4 a = x4[f];
+    consider(a.x, 4 * f);
+    consider(a.y, 4 * f + 1);
+    consider(a.z, 4 * f + 2);
+    consider(a.w, 4 * f + 3);
+  }
+  for (int i = 4 * nvec + threadIdx.x; i < words; i += stride) consider(x[i], i);
   for (int o = 16; o > 0; o >>= 1) {
     float ov = __shfl_xor_sync(0xffffffffu, best, o);
     int oi = __shfl_xor_sync(0xffffffffu, besti, o);

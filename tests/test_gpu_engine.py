@@ -115,12 +115,15 @@ def test_tensor_core_batch_generation_matches_oracle(model_view, model_image):
     e.close()
 
 
-def test_engine_sample_matches_host_sampler(model_view):
+@pytest.mark.parametrize("batch", [False, True])
+def test_engine_sample_matches_host_sampler(model_view, batch):
+    """Per-row SamplingState objects, or one contiguous SamplingStates batch
+    (updated in place)."""
     e = api.InferenceEngine(model_view, max_seqs=2, max_context=64)
     prompts = np.stack([prompt(4, seed=20), prompt(4, seed=21)])
     assert e.prefill_batch([0, 1], prompts, 8)[0] == 0
     rows = [e.logits(0), e.logits(1)]
-    states = [api.SamplingState(7), api.SamplingState(8)]
+    states = api.SamplingStates([7, 8]) if batch else [api.SamplingState(7), api.SamplingState(8)]
     st, ids, errs = e.sample([0, 1], states)
     assert st == 0
     for i in range(2):

@@ -36,6 +36,28 @@ def test_greedy_lowest_id_on_ties():
     assert api.greedy_token(f32bits(logits)) == 3
 
 
+@pytest.mark.parametrize("case", ["ties_across_threads", "signed_zero_max", "last_word", "random_dupes"])
+def test_greedy_first_maximum_matches_oracle(case):
+    """First maximum by strict > (lowest id among equal values, +0 == -0),
+    across the vectorized scan's threads, iterations and tail."""
+    rng = np.random.default_rng(sum(map(ord, case)))
+    logits = (rng.standard_normal(V) * 2.0).astype(np.float32)
+    if case == "ties_across_threads":
+        for i in (4100, 4099, 151000, 4 * 1024 * 4 + 1):
+            logits[i] = np.float32(9.5)
+    elif case == "signed_zero_max":
+        logits = -np.abs(logits) - np.float32(1.0)
+        logits[77777] = np.float32(-0.0)
+        logits[90001] = np.float32(0.0)
+        logits[12] = np.float32(-0.0)
+    elif case == "last_word":
+        logits[V - 1] = np.float32(20.0)
+    else:
+        top = logits.max()
+        logits[rng.choice(V, 6, replace=False)] = top
+    assert api.greedy_token(f32bits(logits)) == oracle.argmax(logits)
+
+
 def test_sampling_known_answer_state():
     logits = f32bits(kat_logits())
     first = api.SamplingState(0x0123456789ABCDEF)
