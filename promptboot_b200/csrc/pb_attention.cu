@@ -1,5 +1,5 @@
-// GQA decode attention for sm_100a, one CTA per (sequence, KV head) serving the
-// KV head's 7 query heads, so every K/V word is read from HBM once.
+// GQA decode attention for sm_100a: every CTA serves the 7 query heads of one
+// KV head, so every K/V word is read from HBM once.
 //
 // Arithmetic of the reference (sulewicz/promptboot fp32_sse2.rs:1430-1672), with
 // every order-sensitive f64 sum kept in the reference's order:
@@ -25,7 +25,9 @@
 //  * attention_pv_kernel: one CTA per (sequence, KV head); the softmax of each
 //    head runs in its warp from the global scores, then V streams through two
 //    64-row buffers while every lane keeps two f64 chains (components 2 lane
-//    and 2 lane + 1, one 8-byte load per position, positions in order).
+//    and 2 lane + 1, one 8-byte load per position, positions in order); the
+//    second chain adds integer-built f64 images of its products instead of
+//    converting them (scaled_product).
 // The probabilities live in shared memory, so this path serves contexts up to
 // kAttnMaxPositions; longer ones use the per-head kernel.
 #include "pb_common.cuh"
@@ -234,7 +236,7 @@ attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
   // 8-byte load per position), positions in order.  Component 2 lane + 1 sums
   // scaled images (scaled_product), valid when every product is finite: the
   // probabilities are (a finite normalizer means every e was finite), and
-  // V is: checked at its write (Batch::kv_checked), or here, where
+  // V is: by the v-projection stage check (Batch::kv_checked), or here, where
   // fma(v, 0, vchk) stays zero while every V word of the chain is finite;
   // otherwise the lane redoes that chain with conversions below.
   double acc0 = 0.0, acc1 = 0.0;
