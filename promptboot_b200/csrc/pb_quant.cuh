@@ -2,6 +2,8 @@
 // produce matvec inputs (RMSNorm, SwiGLU, attention output, the operator API).
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
 
@@ -23,7 +25,8 @@ __device__ __forceinline__ int warp_sum_i32(int v) {
 // ------------------------------------------------------------ Q8_0 quantizer
 
 // fp32_sse2.rs:945-983, one warp per 32-element block: d = amax / 127 rounded to
-// binary16 for storage, inverse from the unrounded d, q = trunc(x * inv +- 0.5).
+// binary16 for storage, inverse from the unrounded d, q = trunc(x * inv +- 0.5)
+// (x86 truncation semantics), stored as its low byte.
 // Returns this lane's quant; dstored = the stored scale (binary16 value as f32).
 __device__ __forceinline__ int quantize_lane(float x, float& dstored) {
   float amax = warp_max_f32(fbits(bitsf(x) & 0x7fffffffu));
@@ -31,8 +34,17 @@ __device__ __forceinline__ int quantize_lane(float x, float& dstored) {
   float inverse = bitsf(d) == 0 ? 0.0f : __fdiv_rn(1.0f, d);
   float v = __fmul_rn(x, inverse);
   float half = (bitsf(v) >> 31) == 0 ? 0.5f : -0.5f;
-  dstored = half_to_f32(f32_to_half(bitsf(d)));
-  return __float2int_rz(__fadd_rn(v, half));
+  // binary16 storage of d: the reference's conversion (fp32_sse2.rs:924-943)
+  // rounds to nearest even and maps +inf to inf, and d is never NaN (amax, like
+  // the reference's strict > scan, skips NaN), so the conversion instruction
+  // gives the same bits, and back exactly.
+  dstored = __half2float(__float2half_rn(d));
+  // fp32_sse2.rs:336-345 truncates with cvttss2si, whose result for a value
+  // outside the int32 range, an infinity or a NaN is 0x80000000 (a block whose
+  // amax is below ~127 * 2^-128 has an infinite inverse); the conversion
+  // instruction here would saturate instead.
+  const float t = __fadd_rn(v, half);
+  return fabsf(t) < 2147483648.0f ? __float2int_rz(t) : (int)0x80000000u;
 }
 
 // Row-major Q8_0 activation (the CUDA-core matvec's input): quants, scale and

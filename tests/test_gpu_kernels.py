@@ -50,6 +50,30 @@ def test_quantizer_matches_fixture_and_oracle():
             assert np.array_equal(got[r], oracle.prepare_q8(x[r])), (cols, r)
 
 
+def test_quantizer_extreme_scales_match_oracle():
+    """Scales d = amax / 127 in the binary16 subnormal range, rounding to zero,
+    overflowing binary16 to inf, and rows with inf / NaN words."""
+    lib = _lib.load()
+    rng = np.random.default_rng(12)
+    rows = []
+    for amax in (127 * 2.0 ** -20, 127 * 2.0 ** -23, 1e-40, 1e-30, 3e-3, 8.3e6, 1e7, 3e38):
+        x = rng.uniform(-1.0, 1.0, 896) * amax
+        x[::32] = amax
+        rows.append(x.astype(np.float32))
+    special = rng.standard_normal(896).astype(np.float32)
+    special[5] = np.inf
+    special[40] = np.nan
+    special[70] = -np.inf
+    rows.append(special)
+    x = np.stack(rows)
+    out = torch.zeros(len(rows) * 28 * 34, dtype=torch.uint8, device="cuda")
+    assert lib.pb_quantize_q8_device(ptr(dev(x)), len(rows), 896, ptr(out), None) == 0
+    sync()
+    got = host(out).reshape(len(rows), -1)
+    for r in range(len(rows)):
+        assert np.array_equal(got[r], oracle.prepare_q8(x[r])), r
+
+
 def test_rmsnorm_matches_fixture_and_oracle():
     lib = _lib.load()
     x = np.array([((i % 17) - 8) / 8.0 for i in range(896)], dtype=np.float32)
