@@ -417,3 +417,102 @@ def test_attention_long_context_matches_oracle(position):
     full[:kv.size] = kv
     ref, _ = oracle.attention(q[0], full, cap, 0, position, (position + 4) & ~3)
     assert np.array_equal(u32(host(out)[0]), u32(ref))
+
+
+def test_swiglu_special_values_match_oracle():
+    """Gate words at expf4's edges (overflow / underflow boundaries, infinities,
+    NaN, signed zeros, subnormals, huge magnitudes) and up words with zeros and
+    infinities; NaN results compared as NaN."""
+    lib = _lib.load()
+    rng = np.random.default_rng(31)
+    g = (rng.standard_normal((3, 4864)) * 30).astype(np.float32)
+    u = rng.standard_normal((3, 4864)).astype(np.float32)
+    specials = np.array([np.inf, -np.inf, np.nan, 0.0, -0.0, 1e-42, -1e-42, 88.72, -88.72,
+                         88.73, -88.73, 103.9, -103.9, 104.0, -104.0, 1e30, -1e30, 3.4e38,
+                         -3.4e38, 126.0, -126.0, 127.0, -127.0], dtype=np.float32)
+    g[0, :specials.size] = specials
+    g[1, 100:100 + specials.size] = specials
+    u[1, 100:100 + specials.size] = np.float32(0.0)
+    g[2, 4000:4000 + specials.size] = specials
+    u[2, 4000:4000 + specials.size] = np.float32(np.inf)
+    out = torch.zeros((3, 4864), dtype=torch.float32, device="cuda")
+    assert lib.pb_swiglu_device(ptr(dev(g)), ptr(dev(u)), 3, ptr(out), None) == 0
+    sync()
+    got = host(out)
+    for r in range(3):
+        assert _same_bits_or_nan(got[r], oracle.swiglu(g[r], u[r])), r
+
+
+def test_rmsnorm_special_rows_match_oracle():
+    """All-zero, subnormal-only, overflowing squares, and rows holding inf or
+    NaN words."""
+    lib = _lib.load()
+    rng = np.random.default_rng(32)
+    rows = [np.zeros(896, dtype=np.float32),
+            (rng.uniform(-1, 1, 896) * 1e-40).astype(np.float32),
+            (rng.standard_normal(896) * 1e20).astype(np.float32),
+            rng.standard_normal(896).astype(np.float32),
+            rng.standard_normal(896).astype(np.float32),
+            rng.standard_normal(896).astype(np.float32)]
+    rows[3][17] = np.inf
+    rows[4][800] = np.nan
+    rows[5][:] = np.float32(-0.0)
+    rows[5][3] = np.float32(2.0 ** -149)
+    xs = np.stack(rows)
+    w = rng.uniform(0.5, 1.5, 896).astype(np.float32)
+    y = torch.zeros((len(rows), 896), dtype=torch.float32, device="cuda")
+    assert lib.pb_rmsnorm_device(ptr(dev(xs)), ptr(dev(w)), len(rows), ptr(y), None) == 0
+    sync()
+    got = host(y)
+    for r in range(len(rows)):
+        assert _same_bits_or_nan(got[r], oracle.rmsnorm(xs[r], w)), r
+
+
+@pytest.mark.parametrize("position", [0, 1, 32766, 32767])
+def test_rope_extreme_positions_match_oracle(position):
+    """The first and the last rows of the 32768-position table."""
+    lib = _lib.load()
+    cap = 32768
+    rng = np.random.default_rng(position + 5)
+    q = (rng.standard_normal((1, 896)) * 4).astype(np.float32)
+    k = (rng.standard_normal((1, 128)) * 4).astype(np.float32)
+    v = rng.standard_normal((1, 128)).astype(np.float32)
+    kv = torch.zeros(24 * 4 * cap * 64 // 24, dtype=torch.float32, device="cuda")  # layer 0 only
+    qd, kd = dev(q), dev(k)
+    pos = np.array([position], dtype=np.uint32)
+    assert lib.pb_rope_kv_device(ptr(qd), ptr(kd), ptr(dev(v)), pos.ctypes.data_as(ctypes.c_void_p),
+                                 1, ptr(kv), cap, 0, None) == 0
+    sync()
+    assert np.array_equal(u32(host(qd)[0]), u32(oracle.rope_in_place(q[0], 14, position)))
+    assert np.array_equal(u32(host(kd)[0]), u32(oracle.rope_in_place(k[0], 2, position)))
+
+
+@pytest.mark.parametrize("case", ["tiny", "huge", "zero_block", "mixed"])
+def test_matvec_extreme_activations_match_oracle(case):
+    """Activations whose Q8_0 blocks hit the quantizer's edges (all-zero blocks,
+    binary16-subnormal scales, scales rounding to inf in binary16) through both
+    matvec paths."""
+    lib = _lib.load()
+    rng = np.random.default_rng(sum(map(ord, case)))
+    rows, cols = 896, 896
+    w = _q4_weights(rng, rows, cols)
+    x = rng.standard_normal((12, cols)).astype(np.float32)
+    if case == "tiny":
+        x *= np.float32(1e-6)
+    elif case == "huge":
+        x *= np.float32(1e6)
+    elif case == "zero_block":
+        x[:, 64:128] = 0.0
+        x[:, 320:352] = np.float32(-0.0)
+    else:
+        x[:, :32] *= np.float32(1e-7)
+        x[:, 32:64] *= np.float32(3e6)
+    for batch in (4, 12):
+        y = torch.zeros((batch, rows), dtype=torch.float32, device="cuda")
+        assert lib.pb_qmatvec_device(2, ptr(dev(w)), rows, cols, ptr(dev(x[:batch])), batch, ptr(y),
+                                     None) == 0
+        sync()
+        got = host(y)
+        for b in range(batch):
+            ref = oracle.q4_matvec(w, oracle.prepare_q8(x[b]), rows, cols)
+            assert _same_bits_or_nan(got[b], ref), (case, batch, b)
