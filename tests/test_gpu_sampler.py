@@ -222,3 +222,53 @@ def test_device_batch_sampler_reports_first_nonfinite_word():
                                               oracle._p(seen))
     master = oracle.SamplingState(24)
     assert got[3, 3] == oracle.sample_top_k_top_p(ref_logits, master.next_24())
+
+
+@pytest.mark.parametrize("case", ["all_equal", "signed_zero_top", "duplicate_top", "penalty_ties"])
+def test_device_batch_sampler_ties_match_oracle(case):
+    """Top-20 ties resolved by the lower id (strict >), signed zeros equal, and
+    ties the repetition penalty creates, against the oracle for 4 rows."""
+    rows = 4
+    rng = np.random.default_rng(sum(map(ord, case)))
+    logits = (rng.standard_normal((rows, V)) * 3.0).astype(np.float32)
+    history = rng.integers(0, V, size=(rows, 512), dtype=np.uint32)
+    if case == "all_equal":
+        logits[:] = np.float32(1.25)
+    elif case == "signed_zero_top":
+        logits = -np.abs(logits) - np.float32(1.0)
+        for r in range(rows):
+            idx = rng.choice(V, 30, replace=False)
+            logits[r, idx[:15]] = np.float32(0.0)
+            logits[r, idx[15:]] = np.float32(-0.0)
+    elif case == "duplicate_top":
+        for r in range(rows):
+            logits[r, rng.choice(V, 40, replace=False)] = np.float32(14.0)
+    else:
+        # x / 1.1 of a penalised token lands exactly on an unpenalised value
+        for r in range(rows):
+            t = int(history[r, 0])
+            logits[r, t] = np.float32(11.0)
+            logits[r, rng.choice(V, 25, replace=False)] = np.float32(np.float32(11.0) / np.float32(1.1))
+    lib = _lib.load()
+    d_logits = dev(logits)
+    master = oracle.SamplingState(99)
+    states = np.zeros((rows, 2), dtype=np.uint64)
+    draws = []
+    for r in range(rows):
+        states[r] = [int(master.state[0]), r]
+        draws.append(master.next_24())
+    out = torch.zeros((rows, 4), dtype=torch.int32, device="cuda")
+    assert lib.pb_sample_batch_device(ptr(d_logits), V, rows, ptr(dev(history.reshape(-1))),
+                                      ptr(dev(np.arange(rows, dtype=np.uint64) * 512)),
+                                      ptr(dev(np.full(rows, 512, dtype=np.uint32))), ptr(dev(states)),
+                                      ptr(out), None) == 0
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint32)
+    mutated = d_logits.cpu().numpy()
+    for r in range(rows):
+        ref_logits = logits[r].copy()
+        seen = np.zeros(api.SEEN_BYTES, dtype=np.uint8)
+        oracle.lib().orc_apply_repetition_penalty(oracle._p(ref_logits), oracle._p(history[r]),
+                                                  512, oracle._p(seen))
+        assert got[r, 0] == 0 and got[r, 3] == oracle.sample_top_k_top_p(ref_logits, draws[r]), r
+        assert np.array_equal(f32bits(mutated[r]), f32bits(ref_logits)), r
