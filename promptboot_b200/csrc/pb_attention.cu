@@ -197,7 +197,10 @@ attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
   float* score = sc + h * span_cap;
   const float* gs = b.scores + ((size_t)row * kQHeads + kh * kHeadsPerKv + h) * b.score_stride;
 
-  // ---- V chunks start streaming while the softmax runs
+  // ---- this head's scores into shared memory (one copy group), then the V
+  // chunks start streaming while the softmax runs
+  for (int i = lane; i < ((positions + 3) >> 2); i += 32) cp_async16(score + 4 * i, gs + 4 * i);
+  cp_commit();
   auto load_v = [&](int t, float* dst) {
     const float* src = vbase + (size_t)t * kChunk * 64;
     const int rows_here = min(kChunk, positions - t * kChunk);
@@ -208,12 +211,14 @@ attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
   if (nchunks > 1) load_v(1, bufs[1]);
   else cp_commit();
 
-  // ---- softmax of head h, entirely within warp h, from the global scores
+  // ---- softmax of head h, entirely within warp h
+  asm volatile("cp.async.wait_group 2;" ::: "memory");  // the scores group has landed
+  __syncwarp();
   float m = fbits(0xff800000u);
-  for (int p = lane; p < positions; p += 32) m = fmaxf(m, gs[p]);
+  for (int p = lane; p < positions; p += 32) m = fmaxf(m, score[p]);
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   for (int p = lane; p < span; p += 32)
-    score[p] = p < positions ? expf4_lane(__fsub_rn(gs[p], m)) : 0.0f;
+    score[p] = p < positions ? expf4_lane(__fsub_rn(score[p], m)) : 0.0f;
   __syncwarp();
   float normalizer = 0.0f;
   if (lane == 0) {
