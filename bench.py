@@ -406,6 +406,15 @@ def algorithmic_bytes(cls: str, seqs: int, start_pos: int, steps: int) -> float:
     return 0.0
 
 
+def step_bytes(seqs: int, start_pos: int, steps: int) -> float:
+    """Algorithmic HBM bytes of one decode step of config 3 averaged over the
+    timed steps: the weights once (346,206,720 B), every sequence's KV of
+    positions 0..pos read (24,576 B each) and this position's written, and its
+    logits row written (607,744 B)."""
+    mean_ctx = start_pos + (steps - 1) / 2.0 + 1.0
+    return 346206720.0 + seqs * (mean_ctx * 24576.0 + 24576.0 + 607744.0)
+
+
 def cpu_baseline(img, threads: int, tokens: int, start: int):
     import oracle
     oracle.bench_decode(img, start, 1, threads, threads)  # page in weights
@@ -561,6 +570,10 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": e2e_value, "unit": UNIT, "steps": e2e_steps,
                     "h2d_bytes_per_step": 36 * S, "d2h_bytes_per_step": 48 * S},
             "gpu_launches": int(launches),
+            "step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes(S, start_pos, args.steps),
+                              "achieved": step_bytes(S, start_pos, args.steps) / (elapsed_ms / args.steps) / 1e6,
+                              "peak": hbm, "unit": "GB/s",
+                              "frac": step_bytes(S, start_pos, args.steps) / (elapsed_ms / args.steps) / 1e6 / hbm},
             "roofline": {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": (achieved / hbm) if achieved else None,
                          "traffic": traffic, "algorithmic_bytes_per_launch": alg_per_launch,
