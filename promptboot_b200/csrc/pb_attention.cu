@@ -79,7 +79,7 @@ struct PvSmem {
   static size_t bytes(int span_cap) { return (size_t)(2 * kVBuf + kHeadsPerKv * span_cap) * 4; }
 };
 
-__global__ void __launch_bounds__(kThreads, 6)
+__global__ void __launch_bounds__(kThreads, 8)
 attention_scores_kernel(Batch b, int layer, const float* rope) {
   pdl_begin();
   __shared__ __align__(16) float qs[kHeadsPerKv * 64];
@@ -316,6 +316,12 @@ int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quant
     cudaFuncSetAttribute(attention_pv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)PvSmem::bytes(kAttnMaxPositions));
     configured = PvSmem::bytes(kAttnMaxPositions);
+  }
+  static bool carved = false;  // one device per process
+  if (!carved) {
+    // 8 score CTAs of 18 KB per SM (the default carveout admits 6)
+    cudaFuncSetAttribute(attention_scores_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    carved = true;
   }
   const int chunks = (span_cap + kChunk - 1) / kChunk;
   launch_pdl(attention_scores_kernel, dim3(chunks, b.rows * 2), kThreads, 0, s, b, layer, rope);
