@@ -309,19 +309,15 @@ int attention_smem_positions() { return kAttnMaxPositions; }
 int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
                              cudaStream_t s) {
   const size_t bytes = PvSmem::bytes(span_cap);
-  static size_t configured = 0;  // one device per process
-  if (bytes > configured) {
+  static std::atomic<uint64_t> configured{0};
+  if (attribute_needed(configured)) {
     cudaFuncSetAttribute(attention_pv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)PvSmem::bytes(kAttnMaxPositions));
     cudaFuncSetAttribute(attention_pv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)PvSmem::bytes(kAttnMaxPositions));
-    configured = PvSmem::bytes(kAttnMaxPositions);
-  }
-  static bool carved = false;  // one device per process
-  if (!carved) {
     // 8 score CTAs of 18 KB per SM (the default carveout admits 6)
     cudaFuncSetAttribute(attention_scores_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    carved = true;
+    attribute_done(configured);
   }
   const int chunks = (span_cap + kChunk - 1) / kChunk;
   launch_pdl(attention_scores_kernel, dim3(chunks, b.rows * 2), kThreads, 0, s, b, layer, rope);

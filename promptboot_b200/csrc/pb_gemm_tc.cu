@@ -525,10 +525,10 @@ qgemm_tc_kernel(TcGemm g, Batch b, unsigned int* status) {
 
 template <bool Q4, class C>
 void launch_tc(const TcGemm& g, const Batch& b, unsigned int* status, cudaStream_t s, int sms) {
-  static bool configured = false;  // one device per process
-  if (!configured) {
+  static std::atomic<uint64_t> configured{0};
+  if (attribute_needed(configured)) {
     cudaFuncSetAttribute(qgemm_tc_kernel<Q4, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kBytes);
-    configured = true;
+    attribute_done(configured);
   }
   const int tiles = g.rtiles * ((b.rows + C::SEQ - 1) / C::SEQ);
   const int grid = std::min(tiles, sms * C::kPerSm);

@@ -3,6 +3,7 @@
 // engine (pb_engine.cu) sequences these per token step.
 #pragma once
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -11,6 +12,19 @@ namespace pb {
 
 // Launches `kernel` with programmatic stream serialization (the kernel begins
 // with pdl_begin()), so its launch and prologue overlap the previous kernel.
+// Kernel attributes belong to a device's context: `done` records the devices
+// (bit per ordinal) whose attribute has been set.  Set first, then mark, so two
+// threads at most both set it (idempotent).
+inline bool attribute_needed(const std::atomic<uint64_t>& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return true;
+  return !(done.load() & (1ull << dev));
+}
+inline void attribute_done(std::atomic<uint64_t>& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) done.fetch_or(1ull << dev);
+}
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                               cudaStream_t s, Args... args) {
