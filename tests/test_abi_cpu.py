@@ -164,3 +164,37 @@ def test_model_open_rejects_bad_layout_before_touching_the_device():
     with pytest.raises(api.ModelError) as e:
         api.ModelView(bad)
     assert e.value.fields == [17, 3, 7, pbtqw25.TENSOR_DIR + 7 * 96 + 8, 2, 3, 18 << 32]
+
+
+def test_sampling_states_batch_shares_one_array():
+    """SamplingStates keeps its rows in one pb_sampling_state array that the
+    batched entry points take as is; items are views of those rows."""
+    from promptboot_b200 import api
+    batch = api.SamplingStates([0, 7, 8])
+    assert len(batch) == 3
+    assert batch[1] == api.SamplingState(7) and batch[-1] == api.SamplingState(8)
+    assert batch[0] == api.SamplingState(0)             # seed 0 takes the replacement constant
+    view = batch[2]
+    view._s.state = 12345
+    assert batch._arr[2].state == 12345                  # a view, not a copy
+    assert api._state_array(batch, 3) is batch._arr
+    with pytest.raises(ValueError):
+        api._state_array(batch, 4)
+    with pytest.raises(IndexError):
+        batch[3]
+    listed = [api.SamplingState(5), api.SamplingState(6)]
+    arr = api._state_array(listed, 2)
+    arr[0].draws = 9
+    api._state_back(listed, arr)
+    assert listed[0].draws() == 9 and listed[1] == api.SamplingState(6)
+
+
+def test_step_views_convert_on_access():
+    from promptboot_b200 import _lib, api
+    arr = (_lib.PbStep * 3)()
+    arr[1].position, arr[1].selected_token, arr[1].eos = 17, 42, 1
+    steps = api._Steps(arr)
+    assert len(steps) == 3
+    assert steps[1].position == 17 and steps[1].selected_token == 42 and steps[1].eos == 1
+    assert [s.position for s in steps] == [0, 17, 0]
+    assert steps[1:][0].selected_token == 42
