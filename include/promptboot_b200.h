@@ -130,6 +130,23 @@ PB_API uint32_t pb_engine_reset_to_prefix(pb_engine *engine, uint32_t seq, uint3
 PB_API uint32_t pb_engine_usage(pb_engine *engine, uint32_t seq, pb_usage *out);
 PB_API uint32_t pb_engine_position(pb_engine *engine, uint32_t seq);
 
+/* KV snapshot access (no counterpart in the reference, whose KV is a caller-
+ * owned byte slice: InferenceEngine::build, inference.rs:977-1011).
+ * pb_engine_kv_device returns the device address of slot `seq`'s KV region,
+ * *words binary32 words = max_context * 6144, in the reference's tiled layout
+ * (inference.rs:2035-2052) with the slot's capacity C in place of 32768:
+ * K at layer*4C*64 + ((h*C/4 + p/4)*64 + c)*4 + p%4, V at layer*4C*64 + 2C*64 +
+ * (h*C + p)*64 + c.  Reads and writes through it are the caller's, ordered
+ * against the engine by synchronizing pb_engine_stream.
+ * pb_engine_restore makes a RESET slot hold `tokens` (n < context limit) whose
+ * KV of positions [0, n) the caller has written there (a saved snapshot):
+ * prefill's prechecks (inference.rs:1109-1191) on tokens and reserve, then the
+ * slot is READY at position n with history = tokens and no greedy id, so the
+ * next call is decode_selected (decode reports the selected-token state error). */
+PB_API void *pb_engine_kv_device(pb_engine *engine, uint32_t seq, uint64_t *words);
+PB_API uint32_t pb_engine_restore(pb_engine *engine, uint32_t seq, const uint32_t *tokens, uint32_t n,
+                                  uint32_t generation_reserve, pb_error *err);
+
 /* Batched forms: one forward step over n distinct sequences at their own
  * positions (a sequence listed twice: PB_CAPACITY).  prefill_batch runs `len`
  * prompt tokens per sequence (tokens is [n][len]; positions but the last as
@@ -212,15 +229,23 @@ PB_API uint32_t pb_qmatvec_device(uint32_t wtype, const uint8_t *w_device, uint3
  * held by each GPU that loads the library; batch is limited to 32 rows and
  * cols to 4864 (PB_CAPACITY otherwise, see pb_last_error_string).  The first
  * call on a device sets it up and should come before any stream capture; all
- * calls share the array, so calls that overlap on the GPU race. */
+ * calls share the array, so calls whose kernels overlap on the GPU (queued on
+ * different streams, from any thread) race; calls queued on one stream are
+ * ordered by it.  Unlike pb_qmatvec_device it does not wait: it returns once
+ * the work is queued on `stream`, and y is ready when that stream has reached
+ * it.  Non-finite outputs are not reported (y holds them as computed).  The
+ * array's device address is looked up once per device for the process, so the
+ * call must not be used after a cudaDeviceReset of that device. */
 PB_API uint32_t pb_qmatvec_device_noalloc(uint32_t wtype, const uint8_t *w_device, uint32_t rows,
                                           uint32_t cols, const float *x_device, uint32_t batch,
                                           float *y_device, void *stream);
-/* y[b] = model tensor `tensor_id` (a layer's q/k/v/o/gate/up/down matrix or the
- * Q8_0 output head, id 290) times the Q8_0-quantized x[b], x f32 [batch][cols]:
+/* y[b] = model tensor `tensor_id` (a layer's q/k/v/o/gate/up/down matrix, the
+ * Q8_0 output head, id 290, or the Q4_0 token embedding, id 0, as a tied
+ * 896 -> 151936 head) times the Q8_0-quantized x[b], x f32 [batch][cols]:
  * the engine's own matvec (the tensor-core path on the model's tile image from
  * 9 rows, the CUDA-core path below).  Asynchronous on `stream`, no per-call
- * allocation once the model's scratch has grown to the batch (batch <= 256);
+ * allocation once the model's scratch has grown to the batch (batch <= 256;
+ * tensor 0's tile image is built on its first call from 9 rows);
  * pb_model_matvec_status synchronizes `stream` and reports a pipeline timeout of
  * any earlier call (PB_DEVICE) once.  Replaces the row loop of
  * inference_q4_matvec_rows_prepared / inference_q8_matvec_rows_prepared
@@ -253,6 +278,9 @@ PB_API uint32_t pb_attention_device(const float *q_device, const float *kv_devic
 /* The 8 MiB RoPE table (32768 x 32 x {cos, sin}) the engine uploads; built from
  * glibc powf/cosf/sinf and checked against the reference's SHA-256. */
 PB_API uint32_t pb_rope_table(float *table_host);
+/* y[i] = the sampler's binary32 exponential of x[i] (bit patterns), the device
+ * routine the top-k/top-p weights use: fp32_sse2.rs:378-469 (scalbnf, expf). */
+PB_API uint32_t pb_expf_device(const uint32_t *x_device, uint64_t n, uint32_t *y_device, void *stream);
 
 #ifdef __cplusplus
 }

@@ -84,7 +84,7 @@ def lib():
             "orc_generate": (u32, [P, P, sz, P, P, u32, u32, ctypes.c_uint64, ctypes.c_int,
                                    P, P, P, P]),
             "orc_generate_many": (u32, [P, sz, P, u32, P, u32, u32, P, u32, P]),
-            "orc_bench_decode": (u32, [P, sz, P, u32, u32, u32, P, u32, P]),
+            "orc_bench_decode": (u32, [P, sz, P, u32, u32, u32, P, u32, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -275,11 +275,18 @@ def cpu_cores() -> int:
 
 
 def bench_decode(model: np.ndarray, start_position: int, steps: int, nseq: int, threads: int,
-                 seeds=None) -> None:
-    """CPU baseline work: nseq sequences x `steps` decode tokens from start_position."""
+                 seeds=None) -> float:
+    """CPU baseline work: nseq sequences x `steps` decode tokens (forward +
+    sampler) from start_position over a seeded KV, on `threads` threads.
+    Returns the aggregate decode rate in tokens/s: all tokens over the summed
+    per-sequence decode-loop time divided by the threads that ran at once (the
+    seeded KV fill before each loop is not timed)."""
     seeds = np.ascontiguousarray(np.arange(nseq) if seeds is None else seeds, dtype=np.uint64)
     cap = ((start_position + steps + 3) // 4) * 4
+    loop = np.zeros(nseq, dtype=np.float64)
     st = lib().orc_bench_decode(_p(model), cap, _p(rope_table()), start_position, steps, nseq,
-                                _p(seeds), threads, None)
+                                _p(seeds), threads, None, _p(loop))
     if st:
         raise RuntimeError(f"oracle bench failed with status {st}")
+    concurrent = max(1, min(threads, nseq))
+    return nseq * steps / (float(loop.sum()) / concurrent)

@@ -13,6 +13,7 @@
 
 #include <math.h>
 #include <pthread.h>
+#include <time.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -670,9 +671,16 @@ typedef struct {
     uint32_t start, steps, nseq;
     const uint64_t *seeds;
     uint32_t *out_tokens;
+    double *loop_seconds;
     uint32_t next;
     pthread_mutex_t lock;
 } orc_bench;
+
+static double now_seconds(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
 
 static void *bench_worker(void *arg) {
     orc_bench *b = (orc_bench *)arg;
@@ -700,6 +708,7 @@ static void *bench_worker(void *arg) {
         uint64_t state = b->seeds[seq] == 0 ? 0x9e3779b97f4a7c15ull : b->seeds[seq], draws = 0;
         uint32_t token = history[b->start - 1];
         orc_error err;
+        const double t0 = now_seconds();
         for (uint32_t t = 0; t < b->steps; ++t) {
             uint32_t pos = b->start + t;
             history[pos] = token;
@@ -711,6 +720,7 @@ static void *bench_worker(void *arg) {
             if (b->out_tokens) b->out_tokens[(size_t)seq * b->steps + t] = sel;
             token = sel;
         }
+        if (b->loop_seconds) b->loop_seconds[seq] = now_seconds() - t0;
     }
     free(s->scores); free(s); free(seen); free(history); free(logits); free(kv);
     return NULL;
@@ -718,12 +728,14 @@ static void *bench_worker(void *arg) {
 
 uint32_t orc_bench_decode(const uint8_t *file, size_t capacity, const float *rope,
                           uint32_t start_position, uint32_t steps, uint32_t nseq,
-                          const uint64_t *seeds, uint32_t threads, uint32_t *out_tokens) {
+                          const uint64_t *seeds, uint32_t threads, uint32_t *out_tokens,
+                          double *loop_seconds) {
     if (start_position == 0 || start_position + steps > capacity) return 2;
     orc_bench b;
     memset(&b, 0, sizeof b);
     b.file = file; b.capacity = capacity; b.rope = rope; b.start = start_position;
     b.steps = steps; b.nseq = nseq; b.seeds = seeds; b.out_tokens = out_tokens;
+    b.loop_seconds = loop_seconds;
     pthread_mutex_init(&b.lock, NULL);
     if (threads < 1) threads = 1;
     pthread_t *tid = (pthread_t *)malloc(threads * sizeof(pthread_t));

@@ -97,7 +97,8 @@ uint32_t orc_generate_many(const uint8_t *file, size_t capacity, const float *ro
  * `steps` tokens (forward + sampler) from start_position over a seeded KV */
 uint32_t orc_bench_decode(const uint8_t *file, size_t capacity, const float *rope,
                           uint32_t start_position, uint32_t steps, uint32_t nseq,
-                          const uint64_t *seeds, uint32_t threads, uint32_t *out_tokens);
+                          const uint64_t *seeds, uint32_t threads, uint32_t *out_tokens,
+                          double *loop_seconds);
 
 #ifdef __cplusplus
 }

@@ -87,6 +87,8 @@ SIGNATURES = {
     "pb_engine_reset_to_prefix": (u32, [P, u32, ctypes.POINTER(u32)]),
     "pb_engine_usage": (u32, [P, u32, ctypes.POINTER(PbUsage)]),
     "pb_engine_position": (u32, [P, u32]),
+    "pb_engine_kv_device": (P, [P, u32, ctypes.POINTER(u64)]),
+    "pb_engine_restore": (u32, [P, u32, P, u32, u32, E]),
     "pb_engine_prefill_batch": (u32, [P, u32, P, P, u32, u32, P, P]),
     "pb_engine_decode_batch": (u32, [P, u32, P, P, u32, P, P]),
     "pb_engine_logits": (u32, [P, u32, P]),
@@ -113,6 +115,7 @@ SIGNATURES = {
     "pb_rope_kv_device": (u32, [P, P, P, P, u32, P, u32, u32, P]),
     "pb_attention_device": (u32, [P, P, u32, u32, P, u32, u32, P, P, P]),
     "pb_rope_table": (u32, [P]),
+    "pb_expf_device": (u32, [P, u64, P, P]),
 }
 
 _LIB = None

@@ -338,6 +338,37 @@ class InferenceEngine:
     def position(self, seq: int = 0) -> int:
         return _lib.load().pb_engine_position(self._h, seq)
 
+    def kv_device(self, seq: int = 0):
+        """(device address, binary32 words) of slot `seq`'s KV region."""
+        words = ctypes.c_uint64()
+        addr = _lib.load().pb_engine_kv_device(self._h, seq, ctypes.byref(words))
+        if not addr:
+            raise IndexError(seq)
+        return int(addr), int(words.value)
+
+    def kv_tensor(self, seq: int = 0):
+        """Slot `seq`'s KV region as a float32 torch tensor sharing the
+        engine's memory (a view through __cuda_array_interface__)."""
+        import torch
+        addr, words = self.kv_device(seq)
+
+        class _Region:
+            __cuda_array_interface__ = {"shape": (words,), "typestr": "<f4",
+                                        "data": (addr, False), "version": 3, "strides": None}
+        return torch.as_tensor(_Region(), device=f"cuda:{self._model.device}")
+
+    def stream(self) -> int:
+        return int(_lib.load().pb_engine_stream(self._h) or 0)
+
+    def restore(self, tokens, generation_reserve: int, seq: int = 0):
+        """A RESET slot takes `tokens` whose KV the caller wrote into its region;
+        it is then READY at position len(tokens) (decode_selected next)."""
+        toks = _u32(tokens)
+        err = _lib.PbError()
+        st = _lib.load().pb_engine_restore(self._h, seq, _ptr(toks), toks.size,
+                                           generation_reserve, ctypes.byref(err))
+        _check(st, err)
+
     # ---- batched forms
     def prefill_batch(self, seqs, tokens: np.ndarray, generation_reserve: int):
         seqs = _u32(seqs)

@@ -504,8 +504,9 @@ struct pb_engine {
           s.emitted = 1;
           steps[i] = publish(s, (uint32_t)r);
           if (n == 1 && host_logits) {
-            PB_CUDA(cudaMemcpy(host_logits, logits + (size_t)r * kVocabWords, kVocabWords * 4,
-                               cudaMemcpyDeviceToHost));
+            PB_CUDA(cudaMemcpyAsync(host_logits, logits + (size_t)r * kVocabWords, kVocabWords * 4,
+                                    cudaMemcpyDeviceToHost, stream));
+            PB_CUDA(cudaStreamSynchronize(stream));
           }
         }
       }
@@ -629,10 +630,11 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   chk(cudaMallocHost(&e->h_greedy, S * 4));
   chk(cudaMallocHost(&e->h_greedy_bits, S * 4));
   if (c == cudaSuccess) pb::init_kernel_attributes();
-  if (c == cudaSuccess) c = cudaMemset(e->kv, 0, S * (size_t)max_context * 6144 * 4);
-  if (c == cudaSuccess) c = cudaMemset(e->history, 0, S * (size_t)max_context * 4);
-  if (c == cudaSuccess) c = cudaMemset(e->d_tc_status, 0, 4);
-  if (c == cudaSuccess) c = cudaMemset(e->aq_tc, 0, pb::tc_act_bytes(e->tc_seqs, 4864));
+  if (c == cudaSuccess) c = cudaMemsetAsync(e->kv, 0, S * (size_t)max_context * 6144 * 4, e->stream);
+  if (c == cudaSuccess) c = cudaMemsetAsync(e->history, 0, S * (size_t)max_context * 4, e->stream);
+  if (c == cudaSuccess) c = cudaMemsetAsync(e->d_tc_status, 0, 4, e->stream);
+  if (c == cudaSuccess) c = cudaMemsetAsync(e->aq_tc, 0, pb::tc_act_bytes(e->tc_seqs, 4864), e->stream);
+  if (c == cudaSuccess) c = cudaStreamSynchronize(e->stream);
   if (c == cudaSuccess) *e->h_tc_status = 0;
   if (c != cudaSuccess) {
     pb::record_cuda_error(c, "pb_engine_create");
@@ -772,7 +774,10 @@ static uint32_t decode_one(pb_engine* e, uint32_t seq, uint32_t token, uint32_t*
   uint32_t status = pb_engine_decode_batch(e, 1, &seq, &token, greedy, &st, &er);
   if (status == PB_OK) {
     if (step) *step = st;
-    if (logits) PB_CUDA(cudaMemcpy(logits, e->logits, 151936 * 4, cudaMemcpyDeviceToHost));
+    if (logits) {
+      PB_CUDA(cudaMemcpyAsync(logits, e->logits, 151936 * 4, cudaMemcpyDeviceToHost, e->stream));
+      PB_CUDA(cudaStreamSynchronize(e->stream));
+    }
   } else {
     if (err) *err = er;
     if (logits && er.status >= PB_NONFINITE_INPUT && e->slots[seq].state == PB_STATE_FAULTED)
@@ -818,7 +823,9 @@ uint32_t pb_engine_prefill_batch(pb_engine* e, uint32_t n, const uint32_t* seqs,
 uint32_t pb_engine_logits(pb_engine* e, uint32_t row, uint32_t* logits) {
   if (!e || !logits || row >= e->last_rows) return PB_CAPACITY;
   cudaSetDevice(e->device);
-  PB_CUDA(cudaMemcpy(logits, e->logits + (size_t)row * 151936, 151936 * 4, cudaMemcpyDeviceToHost));
+  PB_CUDA(cudaMemcpyAsync(logits, e->logits + (size_t)row * 151936, 151936 * 4,
+                          cudaMemcpyDeviceToHost, e->stream));
+  PB_CUDA(cudaStreamSynchronize(e->stream));
   return PB_OK;
 }
 
@@ -867,6 +874,46 @@ uint32_t pb_engine_usage(pb_engine* e, uint32_t seq, pb_usage* out) {
 
 uint32_t pb_engine_position(pb_engine* e, uint32_t seq) {
   return seq_ok(e, seq) ? e->slots[seq].position : 0;
+}
+
+void* pb_engine_kv_device(pb_engine* e, uint32_t seq, uint64_t* words) {
+  if (!seq_ok(e, seq)) {
+    if (words) *words = 0;
+    return nullptr;
+  }
+  const uint64_t per_slot = (uint64_t)e->capacity * 6144ull;
+  if (words) *words = per_slot;
+  return e->kv + (size_t)seq * per_slot;
+}
+
+// A sequence whose KV of positions [0, n) the caller has written into the
+// slot's region (pb_engine_kv_device): prefill's prechecks (inference.rs:
+// 1109-1191) on the tokens and reserve, then the slot holds `tokens` as its
+// history and is READY at position n with no greedy id (decode_selected is the
+// next call; decode reports the reference's selected-token state error).
+uint32_t pb_engine_restore(pb_engine* e, uint32_t seq, const uint32_t* tokens, uint32_t n,
+                           uint32_t reserve, pb_error* err) {
+  if (!seq_ok(e, seq)) { if (err) *err = bad_seq(seq, e ? e->max_seqs : 0); return PB_CAPACITY; }
+  Slot& s = e->slots[seq];
+  pb_error local;
+  pb_error* er = err ? err : &local;
+  if (s.state == PB_STATE_FAULTED) { *er = e->state_error(s, PB_STATE_RESET, 3); return PB_STATE; }
+  if (s.state != PB_STATE_RESET) { *er = e->state_error(s, PB_STATE_RESET, 1); return PB_STATE; }
+  if (!tokens && n) { *er = make_error(PB_CONTEXT, DOM_PROMPT, NO_LAYER, 0, NO_TENSOR, 1, 0, K_CONTEXT, 0); return PB_CONTEXT; }
+  if (!e->prefill_checks(s, tokens, n, reserve, false, er)) return er->status;
+  cudaSetDevice(e->device);
+  PB_CUDA(cudaMemcpyAsync(e->history + (size_t)seq * e->capacity, tokens, (size_t)n * 4,
+                          cudaMemcpyHostToDevice, e->stream));
+  PB_CUDA(cudaStreamSynchronize(e->stream));
+  s.position = n;
+  s.kv_high_water = std::max<uint64_t>(s.kv_high_water, (uint64_t)n * 24576ull);
+  s.scratch_high_water = e->scratch_bytes_per_slot();
+  s.reserve = reserve;
+  s.emitted = 0;
+  s.last_selected = PB_VOCAB;  // no greedy id to continue from
+  s.prefix.clear();
+  s.state = PB_STATE_READY;
+  return PB_OK;
 }
 
 static void sampler_error(pb_error* err, const pb::SamplerRow& r, uint64_t count) {
@@ -979,7 +1026,7 @@ uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
     PB_CUDA(cudaMemcpyAsync(toks.data(), e->d_token_log, (size_t)chunk * n * 4, cudaMemcpyDeviceToHost, e->stream));
     PB_CUDA(cudaMemcpyAsync(e->h_greedy, e->d_greedy, n * 4, cudaMemcpyDeviceToHost, e->stream));
     PB_CUDA(cudaMemcpyAsync(e->h_greedy_bits, e->d_greedy_bits, n * 4, cudaMemcpyDeviceToHost, e->stream));
-    PB_CUDA(cudaMemcpy(e->h_tc_status, e->d_tc_status, 4, cudaMemcpyDeviceToHost));
+    PB_CUDA(cudaMemcpyAsync(e->h_tc_status, e->d_tc_status, 4, cudaMemcpyDeviceToHost, e->stream));
     PB_CUDA(cudaStreamSynchronize(e->stream));
     e->prof_resolve();
     if (e->check_tc_status()) return PB_DEVICE;
@@ -1012,7 +1059,8 @@ uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
       }
     done += chunk;
   }
-  PB_CUDA(cudaMemcpy(states, e->d_states, n * 16, cudaMemcpyDeviceToHost));
+  PB_CUDA(cudaMemcpyAsync(states, e->d_states, n * 16, cudaMemcpyDeviceToHost, e->stream));
+  PB_CUDA(cudaStreamSynchronize(e->stream));
   for (uint32_t i = 0; i < n; ++i)
     if (!failed[i]) e->publish(e->slots[seqs[i]], i);
   e->last_rows = n;

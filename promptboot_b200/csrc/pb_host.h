@@ -51,6 +51,9 @@ struct pb_model {
   uint8_t* tc = nullptr;
   size_t tc_bytes = 0;
   size_t tc_qkv[24] = {}, tc_o[24] = {}, tc_gateup[24] = {}, tc_down[24] = {}, tc_head = 0;
+  // Tile image of the Q4_0 token embedding used as a tied 896 -> 151936 output
+  // head (pb_model_matvec_device on tensor 0), built on its first use.
+  uint8_t* tc_embed = nullptr;
   // Scratch of pb_model_matvec_device (grown on demand) and its pipeline status word.
   uint8_t* op_scratch = nullptr;
   size_t op_scratch_bytes = 0;

@@ -371,6 +371,7 @@ void pb_model_close(pb_model* model) {
   if (model->data) cudaFree(model->data);
   if (model->rope) cudaFree(model->rope);
   if (model->tc) cudaFree(model->tc);
+  if (model->tc_embed) cudaFree(model->tc_embed);
   if (model->op_scratch) cudaFree(model->op_scratch);
   if (model->op_status) cudaFree(model->op_status);
   delete model;

@@ -32,49 +32,100 @@ uint32_t validate_logits(const uint32_t* logits, uint64_t len, pb_error* err) {
   return PB_OK;
 }
 
-// Device buffers for the single-row host-API sampler calls.
+// Device buffers and stream of the single-row host-API sampler calls, kept per
+// host thread and device for the life of the thread: a REPL-style caller
+// (src/model_repl.rs:945-967 in the reference calls the sampler once per token)
+// pays no device allocation per call.  The history buffer grows to the longest
+// history seen so far; everything else has a fixed size.
 struct RowScratch {
+  int device = -1;
+  cudaStream_t stream = nullptr;
   float* logits = nullptr;
   uint32_t* history = nullptr;
+  uint64_t history_words = 0;
   uint64_t* offset = nullptr;
   uint32_t* length = nullptr;
   uint8_t* seen = nullptr;
   unsigned long long* state = nullptr;
   pb::SamplerRow* out = nullptr;
   uint32_t* pairs = nullptr;
-  uint32_t* ids = nullptr;
   ~RowScratch() {
-    void* p[] = {logits, history, offset, length, seen, state, out, pairs, ids};
+    if (device < 0) return;
+    cudaSetDevice(device);
+    void* p[] = {logits, history, offset, length, seen, state, out, pairs};
     for (void* x : p) if (x) cudaFree(x);
+    if (stream) cudaStreamDestroy(stream);
+  }
+  uint32_t setup(int dev) {
+    device = dev;
+    PB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    PB_CUDA(cudaMalloc(&logits, kV * 4));
+    PB_CUDA(cudaMalloc(&offset, 8));
+    PB_CUDA(cudaMalloc(&length, 4));
+    PB_CUDA(cudaMalloc(&state, 16));
+    PB_CUDA(cudaMalloc(&out, sizeof(pb::SamplerRow)));
+    PB_CUDA(cudaMalloc(&seen, PB_SEEN_BYTES));
+    PB_CUDA(cudaMalloc(&pairs, 16 * 4));
+    const uint64_t zero = 0;
+    PB_CUDA(cudaMemcpyAsync(offset, &zero, 8, cudaMemcpyHostToDevice, stream));
+    PB_CUDA(cudaStreamSynchronize(stream));
+    return PB_OK;
+  }
+  uint32_t reserve_history(uint64_t words) {
+    if (words <= history_words) return PB_OK;
+    if (history) PB_CUDA(cudaFree(history));
+    history = nullptr;
+    history_words = 0;
+    const uint64_t grown = std::max<uint64_t>(words, 4096);
+    PB_CUDA(cudaMalloc(&history, grown * 4));
+    history_words = grown;
+    return PB_OK;
   }
 };
+
+// The calling thread's scratch for the current device (set up on first use).
+uint32_t row_scratch(RowScratch** out) {
+  static thread_local RowScratch per_device[64];
+  int dev = 0;
+  PB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    pb::set_last_error("device ordinal out of range");
+    return PB_DEVICE;
+  }
+  RowScratch& s = per_device[dev];
+  if (s.device < 0) {
+    uint32_t st = s.setup(dev);
+    if (st) return st;
+  }
+  *out = &s;
+  return PB_OK;
+}
 
 uint32_t run_sampler_row(uint32_t* logits, const uint32_t* tokens, uint64_t count,
                          const uint8_t* seen, pb_sampling_state* state, pb::SamplerRow* row,
                          bool write_back) {
-  RowScratch s;
-  PB_CUDA(cudaMalloc(&s.logits, kV * 4));
-  PB_CUDA(cudaMalloc(&s.history, std::max<uint64_t>(count, 1) * 4));
-  PB_CUDA(cudaMalloc(&s.offset, 8));
-  PB_CUDA(cudaMalloc(&s.length, 4));
-  PB_CUDA(cudaMalloc(&s.state, 16));
-  PB_CUDA(cudaMalloc(&s.out, sizeof(pb::SamplerRow)));
-  if (seen) PB_CUDA(cudaMalloc(&s.seen, PB_SEEN_BYTES));
-  const uint64_t zero = 0;
+  RowScratch* s = nullptr;
+  uint32_t st = row_scratch(&s);
+  if (st) return st;
+  st = s->reserve_history(count);
+  if (st) return st;
   const uint32_t n = (uint32_t)count;
-  PB_CUDA(cudaMemcpy(s.logits, logits, kV * 4, cudaMemcpyHostToDevice));
-  if (count) PB_CUDA(cudaMemcpy(s.history, tokens, count * 4, cudaMemcpyHostToDevice));
-  PB_CUDA(cudaMemcpy(s.offset, &zero, 8, cudaMemcpyHostToDevice));
-  PB_CUDA(cudaMemcpy(s.length, &n, 4, cudaMemcpyHostToDevice));
-  PB_CUDA(cudaMemcpy(s.state, state, 16, cudaMemcpyHostToDevice));
-  if (seen) PB_CUDA(cudaMemcpy(s.seen, seen, PB_SEEN_BYTES, cudaMemcpyHostToDevice));
-  pb::launch_sampler(s.logits, kV, 1, (int)kV, s.history, s.offset, s.length, s.seen, s.state,
-                     s.out, nullptr);
+  cudaStream_t stream = s->stream;
+  PB_CUDA(cudaMemcpyAsync(s->logits, logits, kV * 4, cudaMemcpyHostToDevice, stream));
+  if (count) PB_CUDA(cudaMemcpyAsync(s->history, tokens, count * 4, cudaMemcpyHostToDevice, stream));
+  PB_CUDA(cudaMemcpyAsync(s->length, &n, 4, cudaMemcpyHostToDevice, stream));
+  PB_CUDA(cudaMemcpyAsync(s->state, state, 16, cudaMemcpyHostToDevice, stream));
+  if (seen) PB_CUDA(cudaMemcpyAsync(s->seen, seen, PB_SEEN_BYTES, cudaMemcpyHostToDevice, stream));
+  pb::launch_sampler(s->logits, kV, 1, (int)kV, s->history, s->offset, s->length,
+                     seen ? s->seen : nullptr, s->state, s->out, stream);
   PB_CUDA(cudaGetLastError());
-  PB_CUDA(cudaMemcpy(row, s.out, sizeof(pb::SamplerRow), cudaMemcpyDeviceToHost));
+  PB_CUDA(cudaMemcpyAsync(row, s->out, sizeof(pb::SamplerRow), cudaMemcpyDeviceToHost, stream));
+  PB_CUDA(cudaStreamSynchronize(stream));
   if (row->status == 0) {
-    PB_CUDA(cudaMemcpy(state, s.state, 16, cudaMemcpyDeviceToHost));
-    if (write_back) PB_CUDA(cudaMemcpy(logits, s.logits, kV * 4, cudaMemcpyDeviceToHost));
+    PB_CUDA(cudaMemcpyAsync(state, s->state, 16, cudaMemcpyDeviceToHost, stream));
+    if (write_back)
+      PB_CUDA(cudaMemcpyAsync(logits, s->logits, kV * 4, cudaMemcpyDeviceToHost, stream));
+    PB_CUDA(cudaStreamSynchronize(stream));
   }
   return PB_OK;
 }
@@ -89,6 +140,12 @@ __global__ void staging_kernel(const int8_t* aq, const float* ad, int rows, int 
   out[0] = (uint8_t)(h & 0xff);
   out[1] = (uint8_t)(h >> 8);
   for (int e = 0; e < 32; ++e) out[2 + e] = (uint8_t)aq[(size_t)r * pb::kActStride + b * 32 + e];
+}
+
+__global__ void expf_kernel(const uint32_t* x, uint64_t n, uint32_t* y) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x)
+    y[i] = pb::bitsf(pb::expf_ref(pb::fbits(x[i])));
 }
 
 __global__ void iota_kernel(int* p, int n) {
@@ -203,14 +260,15 @@ uint32_t pb_sample_token_with_repetition(uint32_t* logits, uint64_t len, const u
 uint32_t pb_greedy_token(const uint32_t* logits, uint64_t len, uint32_t* out, pb_error* err) {
   uint32_t st = validate_logits(logits, len, err);
   if (st) return st;
-  RowScratch s;
-  PB_CUDA(cudaMalloc(&s.logits, kV * 4));
-  PB_CUDA(cudaMalloc(&s.ids, 8));
-  PB_CUDA(cudaMemcpy(s.logits, logits, kV * 4, cudaMemcpyHostToDevice));
-  pb::launch_argmax(s.logits, kV, 1, (int)kV, s.ids, s.ids + 1, nullptr, nullptr);
+  RowScratch* s = nullptr;
+  st = row_scratch(&s);
+  if (st) return st;
+  PB_CUDA(cudaMemcpyAsync(s->logits, logits, kV * 4, cudaMemcpyHostToDevice, s->stream));
+  pb::launch_argmax(s->logits, kV, 1, (int)kV, s->pairs, s->pairs + 1, nullptr, s->stream);
   PB_CUDA(cudaGetLastError());
   uint32_t host[2];
-  PB_CUDA(cudaMemcpy(host, s.ids, 8, cudaMemcpyDeviceToHost));
+  PB_CUDA(cudaMemcpyAsync(host, s->pairs, 8, cudaMemcpyDeviceToHost, s->stream));
+  PB_CUDA(cudaStreamSynchronize(s->stream));
   if (out) *out = host[0];
   return PB_OK;
 }
@@ -218,14 +276,15 @@ uint32_t pb_greedy_token(const uint32_t* logits, uint64_t len, uint32_t* out, pb
 uint32_t pb_top_logits_8(const uint32_t* logits, uint64_t len, pb_top_logit* out8, pb_error* err) {
   uint32_t st = validate_logits(logits, len, err);
   if (st) return st;
-  RowScratch s;
-  PB_CUDA(cudaMalloc(&s.logits, kV * 4));
-  PB_CUDA(cudaMalloc(&s.pairs, 16 * 4));
-  PB_CUDA(cudaMemcpy(s.logits, logits, kV * 4, cudaMemcpyHostToDevice));
-  pb::launch_topk8(s.logits, kV, 1, (int)kV, s.pairs, nullptr, nullptr);
+  RowScratch* s = nullptr;
+  st = row_scratch(&s);
+  if (st) return st;
+  PB_CUDA(cudaMemcpyAsync(s->logits, logits, kV * 4, cudaMemcpyHostToDevice, s->stream));
+  pb::launch_topk8(s->logits, kV, 1, (int)kV, s->pairs, nullptr, s->stream);
   PB_CUDA(cudaGetLastError());
   uint32_t host[16];
-  PB_CUDA(cudaMemcpy(host, s.pairs, sizeof host, cudaMemcpyDeviceToHost));
+  PB_CUDA(cudaMemcpyAsync(host, s->pairs, sizeof host, cudaMemcpyDeviceToHost, s->stream));
+  PB_CUDA(cudaStreamSynchronize(s->stream));
   for (int i = 0; i < 8; ++i) out8[i] = pb_top_logit{host[2 * i], host[2 * i + 1]};
   return PB_OK;
 }
@@ -295,6 +354,10 @@ struct ModelMatrix {
 };
 
 bool model_matrix(const pb_model* m, uint32_t id, ModelMatrix* out) {
+  if (id == 0) {  // the Q4_0 token embedding as a 896 -> 151936 head (tied weights)
+    *out = {pb::W_Q4_0, pb::kVocab, 896, m->tensor(0), m->tc_embed};
+    return true;
+  }
   if (id == 290) {
     *out = {pb::W_Q8_0, pb::kVocab, 896, m->tensor(290), m->tc + m->tc_head};
     return true;
@@ -339,6 +402,13 @@ uint32_t pb_model_matvec_device(pb_model* m, uint32_t id, const float* x, uint32
   if (!m->op_status) {
     PB_CUDA(cudaMalloc(&m->op_status, 4));
     PB_CUDA(cudaMemset(m->op_status, 0, 4));
+  }
+  if (id == 0 && (int)batch >= pb::kTcMinBatch && !m->tc_embed) {
+    PB_CUDA(cudaStreamSynchronize(s));
+    PB_CUDA(cudaMalloc(&m->tc_embed, pb::tc_image_bytes(pb::kVocab, 896)));
+    pb::launch_tc_repack(pb::W_Q4_0, m->tensor(0), pb::kVocab, 896, m->tc_embed, s);
+    PB_CUDA(cudaGetLastError());
+    mm.image = m->tc_embed;
   }
   pb::init_kernel_attributes();
   uint8_t* p = m->op_scratch;
@@ -444,6 +514,14 @@ uint32_t pb_rope_kv_device(float* q, float* k, const float* v, const uint32_t* p
   PB_CUDA(cudaGetLastError());
   PB_CUDA(cudaStreamSynchronize(s));
   PB_CUDA(cudaFree(rope));
+  return PB_OK;
+}
+
+uint32_t pb_expf_device(const uint32_t* x, uint64_t n, uint32_t* y, void* stream) {
+  if (!x || !y || n == 0) return PB_CAPACITY;
+  const uint64_t blocks = std::min<uint64_t>((n + 255) / 256, 148ull * 16);
+  expf_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, n, y);
+  PB_CUDA(cudaGetLastError());
   return PB_OK;
 }
 

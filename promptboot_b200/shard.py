@@ -1,8 +1,9 @@
 """Sequence sharding of the batched decode across ranks (one process per GPU).
 
-The decode path partitions by sequence: rank r of a world of N owns the
-contiguous block of global sequences [r*S, (r+1)*S) (S sequences per rank,
-weak scaling), with its own engine, model replica, KV and sampler states.
+The decode path partitions by sequence: rank r of a world of N owns a
+contiguous block of the global sequences (`partition`: the batch split N ways,
+strong scaling; `global_sequences`: a fixed S per rank, weak scaling), with its
+own engine, model replica, KV and sampler states.
 Nothing is exchanged on the hot path; the only collective is the max of the
 ranks' device-timed durations after the timed region (and barriers around it).
 These helpers are backend-agnostic (NCCL on GPUs, gloo in the CPU tests).
@@ -13,6 +14,18 @@ import numpy as np
 
 PROMPT_SEED = 0x5EED0000   # per-sequence prompt generator: default_rng(PROMPT_SEED + g)
 VOCAB_PROMPT = 151643      # prompt ids uniform in [0, 151643)
+
+
+def partition(total: int, rank: int, world: int) -> tuple[int, int]:
+    """(first global index, count) of rank `rank`'s contiguous block when `total`
+    sequences are split over `world` ranks (strong scaling: the first
+    total % world ranks take one more)."""
+    if not (0 <= rank < world) or total < world:
+        raise ValueError("rank/world/total out of range")
+    base, extra = divmod(total, world)
+    count = base + (1 if rank < extra else 0)
+    first = rank * base + min(rank, extra)
+    return first, count
 
 
 def global_sequences(rank: int, world: int, per_rank: int) -> np.ndarray:

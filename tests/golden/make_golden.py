@@ -8,7 +8,9 @@ are copied byte for byte and each copy is checked against the SHA-256 that the
 reference's provenance file records, so the parity tests can run on machines
 that do not hold the reference tree.
 
-Usage:  python tests/golden/make_golden.py [REFERENCE_ROOT]
+Usage:  python tests/golden/make_golden.py REFERENCE_ROOT
+
+REFERENCE_ROOT is the root of a sulewicz/promptboot checkout.
 """
 from __future__ import annotations
 
@@ -27,7 +29,10 @@ KERNEL_FILES = [
 
 
 def main() -> int:
-    root = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        print("usage: make_golden.py REFERENCE_ROOT (a sulewicz/promptboot checkout)", file=sys.stderr)
+        return 2
+    root = pathlib.Path(sys.argv[1])
     kernels = root / "fixtures" / "inference" / "kernels"
     provenance = json.loads((kernels / "provenance.json").read_text())
     manifest = {}

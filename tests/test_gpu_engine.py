@@ -307,3 +307,33 @@ def test_batched_calls_reject_a_sequence_listed_twice(model_image):
     assert st == 4 and e.position(0) == 3
     e.close()
     view.close()
+
+
+def test_repl_loop_allocates_no_device_memory(model_view):
+    """100 REPL-style iterations (sample_token_with_repetition on host logits,
+    then decode_selected; src/model_repl.rs:945-967) leave the device's free
+    memory unchanged once the first iteration has set up the thread's sampler
+    buffers."""
+    e = api.InferenceEngine(model_view, max_seqs=1, max_context=256)
+    toks = prompt(8, seed=55)
+    logits = np.zeros(api.VOCAB, dtype=np.uint32)
+    e.prefill(toks, 120, logits)
+    seen = np.zeros(api.SEEN_BYTES, dtype=np.uint8)
+    state = api.SamplingState(3)
+    history = list(toks)
+
+    def one():
+        tok = api.sample_token_with_repetition(logits, history, seen, state)
+        history.append(tok)
+        e.decode_selected(tok, logits)
+        api.greedy_token(logits)
+        api.top_logits_8(logits)
+
+    one()
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for _ in range(100):
+        one()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    e.close()

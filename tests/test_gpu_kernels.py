@@ -399,9 +399,9 @@ def test_model_matvec_matches_oracle(model_view, model_image, layer, role, batch
 
 @pytest.mark.parametrize("position", [31023, 20001])
 def test_attention_long_context_matches_oracle(position):
-    """Config 4 scale (SURVEY: 30,000-token prompts + 1,024 decode steps, up to
-    31,024 positions): the global-scores attention path over a seeded KV of
-    slot 0, layer 0, against the oracle."""
+    """Config 4 scale (30,000-token prompts + 1,024 decode steps, up to 31,024
+    positions): the long-context attention path over a seeded KV of slot 0,
+    layer 0, against the oracle."""
     lib = _lib.load()
     cap = 31024
     rng = np.random.default_rng(position)

@@ -55,6 +55,29 @@ def test_noalloc_matches_allocating_operator_on_consecutive_calls(wtype, rows, c
         assert np.array_equal(got, ref), f"call {call}: no-alloc result differs"
 
 
+def test_noalloc_back_to_back_calls_on_a_side_stream():
+    """Two calls queued on one non-default stream with no synchronisation
+    between them (the second overwrites the shared scratch only after the
+    first's kernels are done, by stream order); each output equals the
+    allocating operator's."""
+    lib = _lib.load()
+    rng = np.random.default_rng(11)
+    w = _weights(rng, 2, 896, 4864)
+    xs = [torch.from_numpy(rng.standard_normal((b, 4864)).astype(np.float32)).to("cuda")
+          for b in (32, 3)]
+    refs = [_run(lib.pb_qmatvec_device, 2, w, 896, 4864, x, x.shape[0])[1] for x in xs]
+    side = torch.cuda.Stream()
+    ys = [torch.full((x.shape[0], 896), float("nan"), device="cuda") for x in xs]
+    torch.cuda.synchronize()
+    handle = ctypes.c_void_p(side.cuda_stream)
+    for x, y in zip(xs, ys):
+        assert lib.pb_qmatvec_device_noalloc(2, _ptr(w), 896, 4864, _ptr(x), x.shape[0], _ptr(y),
+                                             handle) == 0
+    side.synchronize()
+    for i, (y, ref) in enumerate(zip(ys, refs)):
+        assert np.array_equal(y.cpu().numpy().view(np.uint32), ref), i
+
+
 def test_noalloc_allocates_nothing_after_setup():
     lib = _lib.load()
     rng = np.random.default_rng(7)
