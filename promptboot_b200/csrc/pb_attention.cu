@@ -29,10 +29,12 @@
 //    second chain adds integer-built f64 images of its products instead of
 //    converting them (scaled_product).
 // The probabilities live in shared memory, so this path serves contexts up to
-// kAttnMaxPositions; longer ones use the per-head kernel.
+// kAttnMaxPositions; longer ones use the long-context launches below.
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
 #include "pb_quant.cuh"
+
+#include <cstdlib>
 
 namespace pb {
 namespace {
@@ -302,9 +304,293 @@ attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
   }
 }
 
+// ------------------------------------------------------------ long contexts
+//
+// Beyond kAttnMaxPositions the probabilities no longer fit in shared memory.
+// The scores come from attention_scores_kernel as above; then
+//  * attention_softmax_long_kernel, one CTA per (sequence, query head): the
+//    maximum, e = expf4(s - max) with the span padded by zeros, the 4-lane
+//    group terms g = fl(fl(e0+e1) + fl(e2+e3)), their f64 sum, and the
+//    probabilities fl(e * f32(1 / sum)) written over the scores.  The sum runs
+//    as a tree when that is provably the reference's serial sum: every g is a
+//    non-negative multiple of 2^L (L = the lowest bit any nonzero g can carry),
+//    so when the total is below 2^(L+53) every partial sum of any grouping is
+//    exactly representable and all orders give the exact total; otherwise one
+//    thread repeats the serial sum in group order.
+//  * attention_pv_long_kernel<G>, one CTA per (sequence, KV head, one of G
+//    component groups): thread (head, component) owns one f64 chain over all
+//    positions in order, V rows of the group and the 7 heads' probabilities
+//    streaming through shared memory, so every V word is read once per KV head
+//    and the 7 x 64 chains of a KV head run on G SMs.
+
+constexpr int kLongThreads = 256;
+
+__global__ void __launch_bounds__(kLongThreads)
+attention_softmax_long_kernel(Batch b) {
+  pdl_begin();
+  __shared__ float wmax[kLongThreads / 32];
+  __shared__ double wsum[kLongThreads / 32];
+  __shared__ int wlow[kLongThreads / 32];
+  __shared__ float normalizer_s;
+  const int row = blockIdx.x / kQHeads, head = blockIdx.x % kQHeads;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int positions = b.positions[row] + 1;
+  const int span = max((positions + 3) & ~3, b.span_min);
+  float* sc = b.scores + ((size_t)row * kQHeads + head) * b.score_stride;
+  float4* sc4 = reinterpret_cast<float4*>(sc);
+  const int groups = span >> 2;
+
+  float m = fbits(0xff800000u);
+  for (int i = tid; i < groups; i += kLongThreads) {
+    const float4 s = sc4[i];
+    const int p = 4 * i;
+    if (p < positions) m = fmaxf(m, s.x);
+    if (p + 1 < positions) m = fmaxf(m, s.y);
+    if (p + 2 < positions) m = fmaxf(m, s.z);
+    if (p + 3 < positions) m = fmaxf(m, s.w);
+  }
+  m = warp_max_f32(m);
+  if (lane == 0) wmax[warp] = m;
+  __syncthreads();
+  m = wmax[0];
+#pragma unroll
+  for (int w = 1; w < kLongThreads / 32; ++w) m = fmaxf(m, wmax[w]);
+
+  // e in place; group terms, their lowest possible bit and a tree partial sum
+  double part = 0.0;
+  int low = 1 << 20;
+  for (int i = tid; i < groups; i += kLongThreads) {
+    const float4 s = sc4[i];
+    const int p = 4 * i;
+    float4 e;
+    e.x = p < positions ? expf4_lane(__fsub_rn(s.x, m)) : 0.0f;
+    e.y = p + 1 < positions ? expf4_lane(__fsub_rn(s.y, m)) : 0.0f;
+    e.z = p + 2 < positions ? expf4_lane(__fsub_rn(s.z, m)) : 0.0f;
+    e.w = p + 3 < positions ? expf4_lane(__fsub_rn(s.w, m)) : 0.0f;
+    sc4[i] = e;
+    const float g = __fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
+    part += (double)g;
+    const uint32_t gb = bitsf(g) & 0x7fffffffu;
+    if (gb != 0) {
+      const int ex = (int)(gb >> 23);
+      low = min(low, ex == 0 ? -149 : ex - 150);
+    }
+  }
+  part = warp_sum_f64(part);
+  for (int o = 16; o > 0; o >>= 1) low = min(low, __shfl_xor_sync(0xffffffffu, low, o));
+  if (lane == 0) {
+    wsum[warp] = part;
+    wlow[warp] = low;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double total = 0.0;
+    int lo = 1 << 20;
+    for (int w = 0; w < kLongThreads / 32; ++w) {
+      total += wsum[w];
+      lo = min(lo, wlow[w]);
+    }
+    // A non-finite or too wide total: the serial sum in group order.  (The
+    // tree's relative error is below 2^-40 for these term counts; the bound
+    // keeps a margin of 2^-30.)
+    const bool exact = lo <= 1000 && total * (1.0 + 0x1p-30) < ldexp(1.0, lo + 53);
+    if (!exact) {
+      double serial = 0.0;
+#pragma unroll 4
+      for (int i = 0; i < groups; ++i) {
+        const float4 e = sc4[i];
+        serial += (double)__fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
+      }
+      total = serial;
+    }
+    normalizer_s = (float)(1.0 / total);
+  }
+  __syncthreads();
+  const float normalizer = normalizer_s;
+  float4* probs = b.probs_out ? reinterpret_cast<float4*>(
+                                    b.probs_out + ((size_t)row * kQHeads + head) * b.score_stride)
+                              : nullptr;
+  for (int i = tid; i < groups; i += kLongThreads) {
+    float4 e = sc4[i];
+    const int p = 4 * i;
+    if (p < positions) e.x = __fmul_rn(e.x, normalizer);
+    if (p + 1 < positions) e.y = __fmul_rn(e.y, normalizer);
+    if (p + 2 < positions) e.z = __fmul_rn(e.z, normalizer);
+    if (p + 3 < positions) e.w = __fmul_rn(e.w, normalizer);
+    sc4[i] = e;
+    if (probs) probs[i] = e;
+  }
+}
+
+// G component groups of 64 / G components; chunk of kLongChunk positions.
+constexpr int kLongChunk = 128;
+
+template <int G>
+struct PvLong {
+  static constexpr int kComps = 64 / G;                           // components per CTA
+  static constexpr int kChains = kHeadsPerKv * kComps;             // 7 heads x components
+  static constexpr int kThreads = (kChains + 31) / 32 * 32;
+  static constexpr int kVWords = kLongChunk * kComps;              // V rows of one chunk
+  static constexpr int kPWords = kHeadsPerKv * kLongChunk;         // probabilities of one chunk
+  static constexpr int kStage = kVWords + kPWords;
+  static constexpr size_t kBytes = 2 * kStage * 4;
+};
+
+template <int G, bool kCheckV>
+__global__ void __launch_bounds__(PvLong<G>::kThreads)
+attention_pv_long_kernel(Batch b, int layer, bool quantize) {
+  using C = PvLong<G>;
+  pdl_begin();
+  extern __shared__ __align__(16) float sm[];
+  const int row = blockIdx.x >> 1, kh = blockIdx.x & 1, grp = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int h = tid / C::kComps, cc = tid % C::kComps;
+  const bool active = tid < C::kChains;
+  const int comp = grp * C::kComps + cc;
+  const int positions = b.positions[row] + 1;
+  const size_t cap = b.capacity;
+  const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
+  const float* vbase = kv + (size_t)layer * 4 * cap * 64 + 2 * cap * 64 + (size_t)kh * cap * 64;
+  const float* probs = b.scores + ((size_t)row * kQHeads + kh * kHeadsPerKv) * b.score_stride;
+  const int nchunks = (positions + kLongChunk - 1) / kLongChunk;
+
+  auto load = [&](int t, float* stage) {
+    const int p0 = t * kLongChunk;
+    const int rows_here = min(kLongChunk, positions - p0);
+    // V rows: kComps words of each position, 16-byte pieces
+    constexpr int kPieces = C::kComps / 4;
+    for (int i = tid; i < rows_here * kPieces; i += C::kThreads) {
+      const int r = i / kPieces, piece = i % kPieces;
+      cp_async16(stage + r * C::kComps + piece * 4,
+                 vbase + (size_t)(p0 + r) * 64 + grp * C::kComps + piece * 4);
+    }
+    // probabilities of the 7 heads (rows_here rounded up to 4: the scratch
+    // holds the padded span)
+    const int quads = (rows_here + 3) >> 2;
+    float* pst = stage + C::kVWords;
+    for (int i = tid; i < kHeadsPerKv * quads; i += C::kThreads) {
+      const int hh = i / quads, q = i % quads;
+      cp_async16(pst + hh * kLongChunk + 4 * q, probs + (size_t)hh * b.score_stride + p0 + 4 * q);
+    }
+    cp_commit();
+  };
+  load(0, sm);
+  if (nchunks > 1) load(1, sm + C::kStage);
+  else cp_commit();
+
+  // Even components convert products on the XU pipe; odd ones sum the
+  // integer-built images of product * 2^-896 (scaled_product), valid while
+  // every product is finite (finite probabilities, and V finite by the
+  // v-projection stage check or by the fma(v, 0, vchk) check here).
+  const bool scaled = (comp & 1) != 0;
+  double acc = 0.0;
+  float vchk = 0.0f;
+  for (int t = 0; t < nchunks; ++t) {
+    cp_wait1();
+    __syncthreads();
+    const float* stage = sm + (t & 1) * C::kStage;
+    const float* vt = stage + cc;
+    const float* pr = stage + C::kVWords + h * kLongChunk;
+    const int rows_here = min(kLongChunk, positions - t * kLongChunk);
+    if (active) {
+      if (scaled) {
+        int i = 0;
+        for (; i + 4 <= rows_here; i += 4) {
+          const float4 p4 = *reinterpret_cast<const float4*>(pr + i);
+          const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float v = vt[(i + j) * C::kComps];
+            acc += scaled_product(pv[j], v);
+            if (kCheckV) vchk = __fmaf_rn(v, 0.0f, vchk);
+          }
+        }
+        for (; i < rows_here; ++i) {
+          const float v = vt[i * C::kComps];
+          acc += scaled_product(pr[i], v);
+          if (kCheckV) vchk = __fmaf_rn(v, 0.0f, vchk);
+        }
+      } else {
+        int i = 0;
+        for (; i + 4 <= rows_here; i += 4) {
+          const float4 p4 = *reinterpret_cast<const float4*>(pr + i);
+          const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc += (double)__fmul_rn(pv[j], vt[(i + j) * C::kComps]);
+        }
+        for (; i < rows_here; ++i) acc += (double)__fmul_rn(pr[i], vt[i * C::kComps]);
+      }
+    }
+    __syncthreads();
+    if (t + 2 < nchunks) load(t + 2, sm + (t & 1) * C::kStage);
+    else cp_commit();
+  }
+  cp_wait0();
+  if (!active) return;
+  const float* hprobs = probs + (size_t)h * b.score_stride;
+  if (scaled) {
+    // probabilities are finite when the normalizer is; the first probability
+    // of a finite normalizer is fl(e * n) with e <= 1, so a non-finite one
+    // shows in any probability word: check position 0's.
+    const float p0 = hprobs[0];
+    if (fabsf(p0) <= 0x1.fffffep127f && vchk == 0.0f) {
+      acc *= 0x1p896;
+    } else {
+      acc = 0.0;
+      for (int p = 0; p < positions; ++p)
+        acc += (double)__fmul_rn(hprobs[p], vbase[(size_t)p * 64 + comp]);
+    }
+  }
+  const float o = (float)acc;
+  const int qh_index = kh * kHeadsPerKv + h;
+  b.attn[(size_t)row * kHidden + qh_index * 64 + comp] = o;
+  check_finite(o, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + comp);
+  if (G == 2 && quantize) {
+    // warp h holds components 32 grp .. 32 grp + 31 of head qh: Q8_0 block
+    // 2 qh + grp of the o-projection input, element = lane
+    quantize_row_block(b, o, row, 2 * qh_index + grp);
+  }
+}
+
 }  // namespace
 
 int attention_smem_positions() { return kAttnMaxPositions; }
+
+// Component groups of the long-context PV launch (PB_ATTN_LONG_GROUPS=2|4|8
+// in the environment selects one for tuning sweeps; tests cover each).
+int attention_long_groups() {
+  if (const char* f = std::getenv("PB_ATTN_LONG_GROUPS")) {
+    const int g = std::atoi(f);
+    if (g == 2 || g == 4 || g == 8) return g;
+  }
+  return 4;
+}
+
+template <int G>
+static void launch_pv_long(const Batch& b, int layer, bool quantize, cudaStream_t s) {
+  using C = PvLong<G>;
+  const dim3 grid(b.rows * 2, G);
+  if (b.kv_checked)
+    launch_pdl(attention_pv_long_kernel<G, false>, grid, C::kThreads, C::kBytes, s, b, layer, quantize);
+  else
+    launch_pdl(attention_pv_long_kernel<G, true>, grid, C::kThreads, C::kBytes, s, b, layer, quantize);
+}
+
+int launch_attention_long(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
+                          cudaStream_t s) {
+  const int chunks = (span_cap + kChunk - 1) / kChunk;
+  launch_pdl(attention_scores_kernel, dim3(chunks, b.rows * 2), kThreads, 0, s, b, layer, rope);
+  launch_pdl(attention_softmax_long_kernel, b.rows * kQHeads, kLongThreads, 0, s, b);
+  const int groups = attention_long_groups();
+  if (groups == 2) launch_pv_long<2>(b, layer, quantize, s);
+  else if (groups == 8) launch_pv_long<8>(b, layer, quantize, s);
+  else launch_pv_long<4>(b, layer, quantize, s);
+  if (quantize && groups != 2) {
+    launch_quant(b, b.attn, kHidden, kHidden, s);
+    return 4;
+  }
+  return 3;
+}
 
 int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
                              cudaStream_t s) {

@@ -360,72 +360,14 @@ void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s
 
 // --------------------------------------------------------------- attention
 //
-// fp32_sse2.rs:1430-1672 for one (sequence, query head) per CTA:
-//   score_p = fl(f32(sum_c f64(fl(q_c * k_pc))) * 0.125)   (c in order, one thread per p)
-//   max over p; span padded to a multiple of 4 with -inf
-//   e = expf4(s - max); sum += f64(fl(fl(e0+e1) + fl(e2+e3))) over 4-groups in order
-//   p = fl(e * f32(1.0 / sum));  out_c = f32(sum_p f64(fl(p * v_pc)))  (p in order)
-// Every order-sensitive f64 sum is sequential as in the reference.
-
-__global__ void attention_kernel(Batch b, int layer) {
-  pdl_begin();
-  __shared__ float qs[64];
-  __shared__ float red[8];
-  __shared__ double total;
-  const int row = blockIdx.x / kQHeads, qh = blockIdx.x % kQHeads, kh = qh / 7;
-  const int positions = b.positions[row] + 1;
-  const int span = max((positions + 3) & ~3, b.span_min);
-  const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * b.capacity * 64;
-  float* sc = b.scores + ((size_t)row * kQHeads + qh) * b.score_stride;
-  if (threadIdx.x < 64) qs[threadIdx.x] = b.q[(size_t)row * kHidden + qh * 64 + threadIdx.x];
-  __syncthreads();
-  float local_max = fbits(0xff800000u);
-  for (int p = threadIdx.x; p < positions; p += blockDim.x) {
-    double dot = 0.0;
-    for (int c = 0; c < 64; ++c)
-      dot += (double)__fmul_rn(qs[c], kv[kv_key_word(b.capacity, layer, kh, p, c)]);
-    float s = __fmul_rn((float)dot, 0.125f);
-    sc[p] = s;
-    if (s > local_max) local_max = s;
-  }
-  local_max = warp_max_f32(local_max);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = local_max;
-  __syncthreads();
-  float maximum = red[0];
-  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) maximum = fmaxf(maximum, red[w]);
-  for (int p = positions + threadIdx.x; p < span; p += blockDim.x) sc[p] = fbits(0xff800000u);
-  __syncthreads();
-  for (int p = threadIdx.x; p < span; p += blockDim.x) sc[p] = expf4_lane(__fsub_rn(sc[p], maximum));
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double sum = 0.0;
-    for (int p = 0; p < span; p += 4)
-      sum += (double)__fadd_rn(__fadd_rn(sc[p], sc[p + 1]), __fadd_rn(sc[p + 2], sc[p + 3]));
-    total = sum;
-  }
-  __syncthreads();
-  const float normalizer = (float)(1.0 / total);
-  for (int p = threadIdx.x; p < positions; p += blockDim.x) sc[p] = __fmul_rn(sc[p], normalizer);
-  __syncthreads();
-  if (threadIdx.x < 64) {
-    const int c = threadIdx.x;
-    double acc = 0.0;
-    for (int p = 0; p < positions; ++p)
-      acc += (double)__fmul_rn(sc[p], kv[kv_value_word(b.capacity, layer, kh, p, c)]);
-    float o = (float)acc;
-    b.attn[(size_t)row * kHidden + qh * 64 + c] = o;
-    check_finite(o, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh * 64 + c);
-  }
-}
+// fp32_sse2.rs:1430-1672, GQA-shared (pb_attention.cu): the shared-memory path
+// up to kAttnMaxPositions, the global-probability path beyond.
 
 int launch_attention(const Batch& b, int layer, int max_span, bool quantize, const float* rope,
                      cudaStream_t s) {
   if (max_span <= kAttnMaxPositions)
     return launch_attention_grouped(b, layer, (max_span + 3) & ~3, quantize, rope, s);
-  if (rope) launch_rope_kv(b, layer, rope, s);
-  launch_pdl(attention_kernel, b.rows * kQHeads, 256, 0, s, b, layer);
-  if (quantize) launch_quant(b, b.attn, kHidden, kHidden, s);
-  return 1 + (rope ? 1 : 0) + (quantize ? 1 : 0);
+  return launch_attention_long(b, layer, (max_span + 3) & ~3, quantize, rope, s);
 }
 
 // -------------------------------------------------------------- argmax/top8

@@ -86,7 +86,7 @@ struct Batch {
 };
 
 // Longest softmax span the shared-memory attention path holds; longer contexts
-// use the per-query-head kernel with global scores.
+// keep the probabilities in the global score scratch.
 constexpr int kAttnMaxPositions = 2048;
 
 enum EpiMode : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
@@ -158,6 +158,10 @@ int launch_attention(const Batch& b, int layer, int max_span, bool quantize, con
                      cudaStream_t s);
 int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
                              cudaStream_t s);
+// Beyond kAttnMaxPositions: scores, then the softmax and the PV chains over
+// probabilities kept in the global score scratch (Batch::scores).
+int launch_attention_long(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
+                          cudaStream_t s);
 void launch_swiglu_quant(const Batch& b, uint32_t layer_ordinal, cudaStream_t s);
 void launch_argmax(const float* logits, size_t ld, int rows, int words, uint32_t* ids,
                    uint32_t* bits, unsigned long long* first_nonfinite, cudaStream_t s);

@@ -275,6 +275,63 @@ def test_attention_extreme_magnitudes_match_oracle(case):
         assert _same_bits_or_nan(got[r], ref), (case, r, positions[r])
 
 
+@pytest.mark.parametrize("groups", ["2", "4", "8"])
+@pytest.mark.parametrize("case", ["random", "wide_scores", "overflowing_products", "inf_value",
+                                  "nan_key", "tiny_values", "wide_values"])
+def test_attention_long_context_extremes_match_oracle(monkeypatch, case, groups):
+    """The long-context path (probabilities in the global scratch, the softmax
+    sum as an exact tree or its serial fallback, PV chains split into 2, 4 or 8
+    component groups) against the oracle, probabilities included: random K/V
+    (the tree sum holds), scores spread over ~200 units (subnormal
+    exponentials: the serial fallback), and the non-finite and extreme cases of
+    the grouped kernels."""
+    monkeypatch.setenv("PB_ATTN_LONG_GROUPS", groups)
+    lib = _lib.load()
+    cap, layer = 3008, 0
+    positions = [2100, 3000]
+    rows = len(positions)
+    rng = np.random.default_rng(sum(map(ord, case)) + int(groups))
+    slot = 24 * 4 * cap * 64
+    kv = np.zeros(rows * slot, dtype=np.float32)
+    q = rng.standard_normal((rows, 896)).astype(np.float32)
+    for r in range(rows):
+        kvr = kv[r * slot:r * slot + 4 * cap * 64]
+        kvr[:] = rng.standard_normal(4 * cap * 64).astype(np.float32)
+        p = positions[r] // 3
+        if case == "wide_scores":
+            q[r] *= np.float32(3.0)
+            for c in range(64):
+                for h in range(2):
+                    kvr[oracle.kv_word(cap, 0, 0, p, h, c)] *= np.float32(40.0)
+        elif case == "overflowing_products":
+            q[r, 7 * 64 + 5] = np.float32(3e19)
+            kvr[oracle.kv_word(cap, 0, 0, p, 1, 5)] = np.float32(2e20)
+        elif case == "inf_value":
+            kvr[oracle.kv_word(cap, 0, 1, p, 0, 17)] = np.float32(np.inf)
+        elif case == "nan_key":
+            kvr[oracle.kv_word(cap, 0, 0, positions[r], 0, 63)] = np.float32(np.nan)
+        elif case == "tiny_values":
+            kvr[2 * cap * 64:] *= np.float32(2.0 ** -128)
+        elif case == "wide_values":
+            e = rng.integers(-140, 31, 2 * cap * 64)
+            kvr[2 * cap * 64:] = (kvr[2 * cap * 64:] * np.exp2(e)).astype(np.float32)
+    span_max = (max(positions) + 4) & ~3
+    out = torch.zeros((rows, 896), dtype=torch.float32, device="cuda")
+    probs = torch.zeros((rows, 14, span_max), dtype=torch.float32, device="cuda")
+    pos = np.array(positions, dtype=np.uint32)
+    assert lib.pb_attention_device(ptr(dev(q)), ptr(dev(kv)), cap, layer,
+                                   pos.ctypes.data_as(ctypes.c_void_p), rows, 0, ptr(out),
+                                   ptr(probs), None) == 0
+    sync()
+    got, got_p = host(out), host(probs)
+    for r in range(rows):
+        span = (positions[r] + 4) & ~3
+        ref, ref_p = oracle.attention(q[r], kv[r * slot:(r + 1) * slot], cap, layer, positions[r],
+                                      span)
+        assert _same_bits_or_nan(got[r], ref), (case, r, positions[r])
+        assert _same_bits_or_nan(got_p[r, 13, :span], ref_p[:span]), (case, r)
+
+
 def _q4_weights(rng, rows, cols):
     nb = rows * cols // 32
     scales = (np.abs(rng.standard_normal(nb) * 0.02) / 8).astype(np.float16)
