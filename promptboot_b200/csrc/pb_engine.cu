@@ -242,8 +242,24 @@ struct pb_engine {
     pb::Epilogue ep;
   };
   void matvec(int wtype, const pb::Batch& b, int columns, const uint8_t* tc_image,
-              std::initializer_list<Mat> mats, int cls) {
+              std::initializer_list<Mat> mats, int cls, int rt = 32) {
     using namespace pb;
+    if (!b.aq_tc) {
+      SmallGemv g{};
+      g.wtype = wtype; g.cols = columns; g.rt = rt;
+      int rows = 0;
+      for (const Mat& m : mats) {
+        rows += m.rows;
+        g.seg[g.nseg].w = m.w;
+        g.seg[g.nseg].rows_end = rows;
+        g.seg[g.nseg].ep = m.ep;
+        ++g.nseg;
+      }
+      if (small_gemv_supported(g, b.rows)) {
+        PB_LAUNCH(cls, launch_small_gemv(g, b, d_tc_status, stream));
+        return;
+      }
+    }
     if (b.aq_tc) {
       TcGemm g{};
       g.wtype = wtype; g.tiles = tc_image; g.nb = columns / 32;
@@ -259,6 +275,22 @@ struct pb_engine {
     } else {
       for (const Mat& m : mats) PB_LAUNCH(cls, launch_qgemv(wtype, m.w, m.rows, columns, b, m.ep, stream));
     }
+  }
+
+  // Small batches: gate and up rows of one 32-row block per CTA, SwiGLU and the
+  // Q8_0 quantization of the products fused into the matvec.
+  bool gateup_swiglu(const pb::Batch& b, const uint8_t* gate_w, const uint8_t* up_w,
+                     const pb::Epilogue& eg, const pb::Epilogue& eu, uint32_t ord) {
+    using namespace pb;
+    SmallGemv g{};
+    g.wtype = W_Q4_0; g.cols = kHidden; g.rt = 32; g.nseg = 2;
+    g.seg[0] = {gate_w, kFfn, eg};
+    g.seg[1] = {up_w, kFfn, eu};
+    g.swiglu = 1;
+    g.swiglu_ordinal = ord;
+    if (!small_gemv_supported(g, b.rows)) return false;
+    PB_LAUNCH(PB_KC_GEMV, launch_small_gemv(g, b, d_tc_status, stream));
+    return true;
   }
 
   // Enqueues one forward step for rows already staged in d_slots/d_positions/
@@ -289,16 +321,20 @@ struct pb_engine {
         PB_LAUNCH_N(PB_KC_ATTENTION, launch_attention(b, layer, max_span, true, nullptr, stream));
       }
       const Epilogue eo{EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_ATTN_OUTPUT};
-      matvec(W_Q4_0, b, 896, m->tc + m->tc_o[layer], {{T(17), 896, eo}}, PB_KC_GEMV);
+      matvec(W_Q4_0, b, 896, m->tc + m->tc_o[layer], {{T(17), 896, eo}}, PB_KC_GEMV, 8);
       PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(T(14)), ord,
                                                  D_FFN_NORM, stream));
       const Epilogue eg{EPI_STORE, gate, kFfn, nullptr, err, ord, D_GATE};
       const Epilogue eu{EPI_STORE, up, kFfn, nullptr, err, ord, D_UP};
-      matvec(W_Q4_0, b, 896, m->tc + m->tc_gateup[layer], {{T(12), 4864, eg}, {T(13), 4864, eu}},
-             PB_KC_GEMV);
-      PB_LAUNCH(PB_KC_SWIGLU, launch_swiglu_quant(b, ord, stream));
+      if (!b.aq_tc && gateup_swiglu(b, T(12), T(13), eg, eu, ord)) {
+        // gate/up, SwiGLU and its quantization in one small-batch launch
+      } else {
+        matvec(W_Q4_0, b, 896, m->tc + m->tc_gateup[layer], {{T(12), 4864, eg}, {T(13), 4864, eu}},
+               PB_KC_GEMV);
+        PB_LAUNCH(PB_KC_SWIGLU, launch_swiglu_quant(b, ord, stream));
+      }
       const Epilogue ed{EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_DOWN};
-      matvec(W_Q4_0, b, 4864, m->tc + m->tc_down[layer], {{T(11), 896, ed}}, PB_KC_GEMV);
+      matvec(W_Q4_0, b, 4864, m->tc + m->tc_down[layer], {{T(11), 896, ed}}, PB_KC_GEMV, 8);
     }
     if (want_logits) {
       PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(m->tensor(289)),

@@ -147,6 +147,28 @@ struct TcGemm {
 int tc_pick_config(int rtiles, int batch);
 // Sets *status (device word) if a pipeline wait timed out.
 void launch_tc_gemm(const TcGemm& g, const Batch& b, unsigned int* status, cudaStream_t s);
+// Small-batch (B <= 8) matvec on CUDA cores (pb_gemv_small.cu): up to three
+// matrices stacked by rows (segment i covers launch rows [seg[i-1].rows_end,
+// seg[i].rows_end) and reads seg[i].w from its row 0), or in SwiGLU mode a
+// gate/up pair (seg[0] gate, seg[1] up, the same 4864 rows) whose products are
+// SwiGLU'd and quantized to the row-major Q8_0 activation.  rt rows per CTA
+// (32 in SwiGLU mode) must divide every segment.
+struct SmallGemv {
+  int wtype;
+  int cols;
+  int rt;
+  int nseg;
+  struct Seg {
+    const uint8_t* w;
+    int rows_end;
+    Epilogue ep;
+  } seg[3];
+  int swiglu;
+  uint32_t swiglu_ordinal;
+};
+bool small_gemv_supported(const SmallGemv& g, int batch);
+// Sets *status (device word) if a weight copy did not land in time.
+void launch_small_gemv(const SmallGemv& g, const Batch& b, unsigned int* status, cudaStream_t s);
 void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s);
 // max_span: the largest softmax span of the batch, (position + 4) & ~3 (or span_min).
 // quantize: also write the Q8_0 activation of the output (the o-projection input).

@@ -430,7 +430,13 @@ uint32_t pb_model_matvec_device(pb_model* m, uint32_t id, const float* x, uint32
     pb::launch_tc_gemm(g, b, m->op_status, s);
   } else {
     pb::launch_quant(b, x, mm.cols, mm.cols, s);
-    pb::launch_qgemv(mm.wtype, mm.w, mm.rows, mm.cols, b, ep, s);
+    pb::SmallGemv g{};
+    g.wtype = mm.wtype; g.cols = mm.cols; g.rt = mm.cols > 896 ? 8 : 32; g.nseg = 1;
+    g.seg[0].w = mm.w; g.seg[0].rows_end = mm.rows; g.seg[0].ep = ep;
+    if (pb::small_gemv_supported(g, (int)batch))
+      pb::launch_small_gemv(g, b, m->op_status, s);
+    else
+      pb::launch_qgemv(mm.wtype, mm.w, mm.rows, mm.cols, b, ep, s);
   }
   PB_CUDA(cudaGetLastError());
   return PB_OK;
