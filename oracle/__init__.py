@@ -15,6 +15,7 @@ import ctypes
 import os
 import pathlib
 import subprocess
+import threading
 
 import numpy as np
 
@@ -46,9 +47,18 @@ def build() -> pathlib.Path:
 
 
 _LIB = None
+_INIT_LOCK = threading.RLock()
 
 
 def lib():
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _INIT_LOCK:
+        return _load()
+
+
+def _load():
     global _LIB
     if _LIB is None:
         if not LIB_PATH.exists():
@@ -159,11 +169,15 @@ _ROPE = None
 
 
 def rope_table() -> np.ndarray:
+    """The inference RoPE table, built once per process.  Callers pass its raw
+    address to C, so the table must never be replaced once published: threads
+    that race here build it under a lock."""
     global _ROPE
-    if _ROPE is None:
-        t = np.zeros(ROPE_WORDS, dtype=np.float32)
-        lib().orc_rope_table(_p(t))
-        _ROPE = t
+    with _INIT_LOCK:
+        if _ROPE is None:
+            t = np.zeros(ROPE_WORDS, dtype=np.float32)
+            lib().orc_rope_table(_p(t))
+            _ROPE = t
     return _ROPE
 
 
