@@ -270,6 +270,8 @@ PB_API uint32_t pb_rope_kv_device(float *q_device, float *k_device, const float 
                            uint32_t capacity, uint32_t layer, void *stream);
 /* GQA decode attention (fp32_sse2.rs:1430-1672) of q [rows][896] over the KV of
  * slot r at current positions[r]; span (0 = natural) pads the softmax span.
+ * capacity and span at most 32768 (the reference's context), capacity a
+ * multiple of 4 (PB_CAPACITY otherwise).
  * scores_device (optional) receives [rows][14][span_max] final probabilities. */
 PB_API uint32_t pb_attention_device(const float *q_device, const float *kv_device, uint32_t capacity,
                              uint32_t layer, const uint32_t *positions_host, uint32_t rows,

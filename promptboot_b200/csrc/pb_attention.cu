@@ -316,14 +316,19 @@ attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
 //    non-negative multiple of 2^L (L = the lowest bit any nonzero g can carry),
 //    so when the total is below 2^(L+53) every partial sum of any grouping is
 //    exactly representable and all orders give the exact total; otherwise one
-//    thread repeats the serial sum in group order.
+//    thread repeats the serial sum in group order over the terms kept in
+//    shared memory.
 //  * attention_pv_long_kernel<G>, one CTA per (sequence, KV head, one of G
-//    component groups): thread (head, component) owns one f64 chain over all
-//    positions in order, V rows of the group and the 7 heads' probabilities
-//    streaming through shared memory, so every V word is read once per KV head
-//    and the 7 x 64 chains of a KV head run on G SMs.
+//    component groups): a thread owns the two f64 chains of components
+//    (2 c, 2 c + 1) of one head over all positions in order, V rows of the
+//    group and the 7 heads' probabilities streaming through shared memory, so
+//    every V word is read once per KV head and the 7 x 64 chains of a KV head
+//    run on G SMs.  Each chain is one dependent f64 add per position (8.2
+//    cycles measured on B200): at 31k positions that latency, not HBM, bounds
+//    the launch.
 
 constexpr int kLongThreads = 256;
+constexpr int kLongMaxGroups = kContextLimit / 4;  // spans of at most 32768 positions
 
 __global__ void __launch_bounds__(kLongThreads)
 attention_softmax_long_kernel(Batch b) {
@@ -332,6 +337,7 @@ attention_softmax_long_kernel(Batch b) {
   __shared__ double wsum[kLongThreads / 32];
   __shared__ int wlow[kLongThreads / 32];
   __shared__ float normalizer_s;
+  __shared__ float gterm[kLongMaxGroups];  // group terms for the serial fallback
   const int row = blockIdx.x / kQHeads, head = blockIdx.x % kQHeads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int positions = b.positions[row] + 1;
@@ -369,6 +375,7 @@ attention_softmax_long_kernel(Batch b) {
     e.w = p + 3 < positions ? expf4_lane(__fsub_rn(s.w, m)) : 0.0f;
     sc4[i] = e;
     const float g = __fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
+    gterm[i] = g;
     part += (double)g;
     const uint32_t gb = bitsf(g) & 0x7fffffffu;
     if (gb != 0) {
@@ -396,11 +403,8 @@ attention_softmax_long_kernel(Batch b) {
     const bool exact = lo <= 1000 && total * (1.0 + 0x1p-30) < ldexp(1.0, lo + 53);
     if (!exact) {
       double serial = 0.0;
-#pragma unroll 4
-      for (int i = 0; i < groups; ++i) {
-        const float4 e = sc4[i];
-        serial += (double)__fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
-      }
+#pragma unroll 8
+      for (int i = 0; i < groups; ++i) serial += (double)gterm[i];
       total = serial;
     }
     normalizer_s = (float)(1.0 / total);
@@ -422,31 +426,38 @@ attention_softmax_long_kernel(Batch b) {
   }
 }
 
-// G component groups of 64 / G components; chunk of kLongChunk positions.
+// G component groups of 64 / G components per CTA; a thread owns the two
+// chains of components (2 c, 2 c + 1) of one head, the first converting its
+// products on the XU pipe, the second summing integer-built images
+// (scaled_product), like attention_pv_kernel.  kLongStages chunks of
+// kLongChunk positions are in flight (V rows of the group and the 7 heads'
+// probabilities, cp.async into shared memory).
 constexpr int kLongChunk = 128;
+constexpr int kLongStages = 4;
 
 template <int G>
 struct PvLong {
   static constexpr int kComps = 64 / G;                           // components per CTA
-  static constexpr int kChains = kHeadsPerKv * kComps;             // 7 heads x components
-  static constexpr int kThreads = (kChains + 31) / 32 * 32;
+  static constexpr int kPairs = kComps / 2;                       // threads per head
+  static constexpr int kWorkers = kHeadsPerKv * kPairs;
+  static constexpr int kThreads = (kWorkers + 31) / 32 * 32;
   static constexpr int kVWords = kLongChunk * kComps;              // V rows of one chunk
   static constexpr int kPWords = kHeadsPerKv * kLongChunk;         // probabilities of one chunk
   static constexpr int kStage = kVWords + kPWords;
-  static constexpr size_t kBytes = 2 * kStage * 4;
+  static constexpr size_t kBytes = (size_t)kLongStages * kStage * 4;
 };
 
 template <int G, bool kCheckV>
 __global__ void __launch_bounds__(PvLong<G>::kThreads)
-attention_pv_long_kernel(Batch b, int layer, bool quantize) {
+attention_pv_long_kernel(Batch b, int layer) {
   using C = PvLong<G>;
   pdl_begin();
   extern __shared__ __align__(16) float sm[];
   const int row = blockIdx.x >> 1, kh = blockIdx.x & 1, grp = blockIdx.y;
   const int tid = threadIdx.x;
-  const int h = tid / C::kComps, cc = tid % C::kComps;
-  const bool active = tid < C::kChains;
-  const int comp = grp * C::kComps + cc;
+  const int h = tid / C::kPairs, c2 = tid % C::kPairs;
+  const bool active = tid < C::kWorkers;
+  const int comp = grp * C::kComps + 2 * c2;  // this thread's first component
   const int positions = b.positions[row] + 1;
   const size_t cap = b.capacity;
   const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
@@ -454,107 +465,121 @@ attention_pv_long_kernel(Batch b, int layer, bool quantize) {
   const float* probs = b.scores + ((size_t)row * kQHeads + kh * kHeadsPerKv) * b.score_stride;
   const int nchunks = (positions + kLongChunk - 1) / kLongChunk;
 
-  auto load = [&](int t, float* stage) {
-    const int p0 = t * kLongChunk;
-    const int rows_here = min(kLongChunk, positions - p0);
-    // V rows: kComps words of each position, 16-byte pieces
-    constexpr int kPieces = C::kComps / 4;
-    for (int i = tid; i < rows_here * kPieces; i += C::kThreads) {
-      const int r = i / kPieces, piece = i % kPieces;
-      cp_async16(stage + r * C::kComps + piece * 4,
-                 vbase + (size_t)(p0 + r) * 64 + grp * C::kComps + piece * 4);
+  auto load = [&](int t) {
+    if (t < nchunks) {
+      float* stage = sm + (t % kLongStages) * C::kStage;
+      const int p0 = t * kLongChunk;
+      const int rows_here = min(kLongChunk, positions - p0);
+      constexpr int kPieces = C::kComps / 4;
+      for (int i = tid; i < rows_here * kPieces; i += C::kThreads) {
+        const int r = i / kPieces, piece = i % kPieces;
+        cp_async16(stage + r * C::kComps + piece * 4,
+                   vbase + (size_t)(p0 + r) * 64 + grp * C::kComps + piece * 4);
+      }
+      // probabilities of the 7 heads, rows_here rounded up to 4 (the scratch
+      // holds the padded span)
+      const int quads = (rows_here + 3) >> 2;
+      float* pst = stage + C::kVWords;
+      for (int i = tid; i < kHeadsPerKv * quads; i += C::kThreads) {
+        const int hh = i / quads, q = i % quads;
+        cp_async16(pst + hh * kLongChunk + 4 * q, probs + (size_t)hh * b.score_stride + p0 + 4 * q);
+      }
     }
-    // probabilities of the 7 heads (rows_here rounded up to 4: the scratch
-    // holds the padded span)
-    const int quads = (rows_here + 3) >> 2;
-    float* pst = stage + C::kVWords;
-    for (int i = tid; i < kHeadsPerKv * quads; i += C::kThreads) {
-      const int hh = i / quads, q = i % quads;
-      cp_async16(pst + hh * kLongChunk + 4 * q, probs + (size_t)hh * b.score_stride + p0 + 4 * q);
-    }
-    cp_commit();
+    cp_commit();  // one group per chunk slot, empty past the end
   };
-  load(0, sm);
-  if (nchunks > 1) load(1, sm + C::kStage);
-  else cp_commit();
+#pragma unroll
+  for (int t = 0; t < kLongStages - 1; ++t) load(t);
 
-  // Even components convert products on the XU pipe; odd ones sum the
-  // integer-built images of product * 2^-896 (scaled_product), valid while
-  // every product is finite (finite probabilities, and V finite by the
-  // v-projection stage check or by the fma(v, 0, vchk) check here).
-  const bool scaled = (comp & 1) != 0;
-  double acc = 0.0;
+  double acc0 = 0.0, acc1 = 0.0;
   float vchk = 0.0f;
   for (int t = 0; t < nchunks; ++t) {
-    cp_wait1();
+    load(t + kLongStages - 1);
+    asm volatile("cp.async.wait_group %0;" ::"n"(kLongStages - 1) : "memory");
     __syncthreads();
-    const float* stage = sm + (t & 1) * C::kStage;
-    const float* vt = stage + cc;
+    const float* stage = sm + (t % kLongStages) * C::kStage;
+    const float* vt = stage + 2 * c2;  // this thread's component pair in each V row
     const float* pr = stage + C::kVWords + h * kLongChunk;
     const int rows_here = min(kLongChunk, positions - t * kLongChunk);
     if (active) {
-      if (scaled) {
-        int i = 0;
-        for (; i + 4 <= rows_here; i += 4) {
-          const float4 p4 = *reinterpret_cast<const float4*>(pr + i);
-          const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+      int i = 0;
+      for (; i + 8 <= rows_here; i += 8) {
+        const float4 pa = *reinterpret_cast<const float4*>(pr + i);
+        const float4 pb = *reinterpret_cast<const float4*>(pr + i + 4);
+        const float pv[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+        float2 v[8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float v = vt[(i + j) * C::kComps];
-            acc += scaled_product(pv[j], v);
-            if (kCheckV) vchk = __fmaf_rn(v, 0.0f, vchk);
-          }
-        }
-        for (; i < rows_here; ++i) {
-          const float v = vt[i * C::kComps];
-          acc += scaled_product(pr[i], v);
-          if (kCheckV) vchk = __fmaf_rn(v, 0.0f, vchk);
-        }
-      } else {
-        int i = 0;
-        for (; i + 4 <= rows_here; i += 4) {
-          const float4 p4 = *reinterpret_cast<const float4*>(pr + i);
-          const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+        for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const float2*>(vt + (i + j) * C::kComps);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc += (double)__fmul_rn(pv[j], vt[(i + j) * C::kComps]);
+        for (int j = 0; j < 8; ++j) {
+          acc0 += (double)__fmul_rn(pv[j], v[j].x);
+          acc1 += scaled_product(pv[j], v[j].y);
+          if (kCheckV) vchk = __fmaf_rn(v[j].y, 0.0f, vchk);
         }
-        for (; i < rows_here; ++i) acc += (double)__fmul_rn(pr[i], vt[i * C::kComps]);
+      }
+      for (; i < rows_here; ++i) {
+        const float2 v = *reinterpret_cast<const float2*>(vt + i * C::kComps);
+        acc0 += (double)__fmul_rn(pr[i], v.x);
+        acc1 += scaled_product(pr[i], v.y);
+        if (kCheckV) vchk = __fmaf_rn(v.y, 0.0f, vchk);
       }
     }
-    __syncthreads();
-    if (t + 2 < nchunks) load(t + 2, sm + (t & 1) * C::kStage);
-    else cp_commit();
+    __syncthreads();  // the slot is refilled by the next iteration's load
   }
-  cp_wait0();
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   if (!active) return;
   const float* hprobs = probs + (size_t)h * b.score_stride;
-  if (scaled) {
-    // probabilities are finite when the normalizer is; the first probability
-    // of a finite normalizer is fl(e * n) with e <= 1, so a non-finite one
-    // shows in any probability word: check position 0's.
-    const float p0 = hprobs[0];
-    if (fabsf(p0) <= 0x1.fffffep127f && vchk == 0.0f) {
-      acc *= 0x1p896;
-    } else {
-      acc = 0.0;
-      for (int p = 0; p < positions; ++p)
-        acc += (double)__fmul_rn(hprobs[p], vbase[(size_t)p * 64 + comp]);
-    }
+  // The scaled chain needs finite products: finite probabilities (a finite
+  // normalizer; a non-finite one shows in every probability word, position
+  // 0's included) and finite V (the v-projection check, or vchk here).
+  const float p0 = hprobs[0];
+  if (fabsf(p0) <= 0x1.fffffep127f && vchk == 0.0f) {
+    acc1 *= 0x1p896;
+  } else {
+    acc1 = 0.0;
+    for (int p = 0; p < positions; ++p)
+      acc1 += (double)__fmul_rn(hprobs[p], vbase[(size_t)p * 64 + comp + 1]);
   }
-  const float o = (float)acc;
+  const float o0 = (float)acc0, o1 = (float)acc1;
   const int qh_index = kh * kHeadsPerKv + h;
-  b.attn[(size_t)row * kHidden + qh_index * 64 + comp] = o;
-  check_finite(o, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + comp);
-  if (G == 2 && quantize) {
-    // warp h holds components 32 grp .. 32 grp + 31 of head qh: Q8_0 block
-    // 2 qh + grp of the o-projection input, element = lane
-    quantize_row_block(b, o, row, 2 * qh_index + grp);
-  }
+  *reinterpret_cast<float2*>(b.attn + (size_t)row * kHidden + qh_index * 64 + comp) =
+      make_float2(o0, o1);
+  check_finite(o0, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + comp);
+  check_finite(o1, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + comp + 1);
 }
 
 }  // namespace
 
 int attention_smem_positions() { return kAttnMaxPositions; }
+
+void configure_scores_kernel() {
+  static std::atomic<uint64_t> configured{0};
+  if (attribute_needed(configured)) {
+    // 8 score CTAs of 18 KB per SM (the default carveout admits 6)
+    cudaFuncSetAttribute(attention_scores_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    attribute_done(configured);
+  }
+}
+
+int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
+                             cudaStream_t s) {
+  const size_t bytes = PvSmem::bytes(span_cap);
+  static std::atomic<uint64_t> configured{0};
+  if (attribute_needed(configured)) {
+    cudaFuncSetAttribute(attention_pv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)PvSmem::bytes(kAttnMaxPositions));
+    cudaFuncSetAttribute(attention_pv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)PvSmem::bytes(kAttnMaxPositions));
+    attribute_done(configured);
+  }
+  configure_scores_kernel();
+  const int chunks = (span_cap + kChunk - 1) / kChunk;
+  launch_pdl(attention_scores_kernel, dim3(chunks, b.rows * 2), kThreads, 0, s, b, layer, rope);
+  if (b.kv_checked)
+    launch_pdl(attention_pv_kernel<false>, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
+  else
+    launch_pdl(attention_pv_kernel<true>, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
+  return 2;
+}
 
 // Component groups of the long-context PV launch (PB_ATTN_LONG_GROUPS=2|4|8
 // in the environment selects one for tuning sweeps; tests cover each).
@@ -567,51 +592,38 @@ int attention_long_groups() {
 }
 
 template <int G>
-static void launch_pv_long(const Batch& b, int layer, bool quantize, cudaStream_t s) {
+static void launch_pv_long(const Batch& b, int layer, cudaStream_t s) {
   using C = PvLong<G>;
+  static std::atomic<uint64_t> configured{0};
+  if (attribute_needed(configured)) {
+    cudaFuncSetAttribute(attention_pv_long_kernel<G, false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kBytes);
+    cudaFuncSetAttribute(attention_pv_long_kernel<G, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kBytes);
+    attribute_done(configured);
+  }
   const dim3 grid(b.rows * 2, G);
   if (b.kv_checked)
-    launch_pdl(attention_pv_long_kernel<G, false>, grid, C::kThreads, C::kBytes, s, b, layer, quantize);
+    launch_pdl(attention_pv_long_kernel<G, false>, grid, C::kThreads, C::kBytes, s, b, layer);
   else
-    launch_pdl(attention_pv_long_kernel<G, true>, grid, C::kThreads, C::kBytes, s, b, layer, quantize);
+    launch_pdl(attention_pv_long_kernel<G, true>, grid, C::kThreads, C::kBytes, s, b, layer);
 }
 
 int launch_attention_long(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
                           cudaStream_t s) {
+  configure_scores_kernel();
   const int chunks = (span_cap + kChunk - 1) / kChunk;
   launch_pdl(attention_scores_kernel, dim3(chunks, b.rows * 2), kThreads, 0, s, b, layer, rope);
   launch_pdl(attention_softmax_long_kernel, b.rows * kQHeads, kLongThreads, 0, s, b);
   const int groups = attention_long_groups();
-  if (groups == 2) launch_pv_long<2>(b, layer, quantize, s);
-  else if (groups == 8) launch_pv_long<8>(b, layer, quantize, s);
-  else launch_pv_long<4>(b, layer, quantize, s);
-  if (quantize && groups != 2) {
+  if (groups == 2) launch_pv_long<2>(b, layer, s);
+  else if (groups == 8) launch_pv_long<8>(b, layer, s);
+  else launch_pv_long<4>(b, layer, s);
+  if (quantize) {
     launch_quant(b, b.attn, kHidden, kHidden, s);
     return 4;
   }
   return 3;
-}
-
-int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
-                             cudaStream_t s) {
-  const size_t bytes = PvSmem::bytes(span_cap);
-  static std::atomic<uint64_t> configured{0};
-  if (attribute_needed(configured)) {
-    cudaFuncSetAttribute(attention_pv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)PvSmem::bytes(kAttnMaxPositions));
-    cudaFuncSetAttribute(attention_pv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)PvSmem::bytes(kAttnMaxPositions));
-    // 8 score CTAs of 18 KB per SM (the default carveout admits 6)
-    cudaFuncSetAttribute(attention_scores_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attribute_done(configured);
-  }
-  const int chunks = (span_cap + kChunk - 1) / kChunk;
-  launch_pdl(attention_scores_kernel, dim3(chunks, b.rows * 2), kThreads, 0, s, b, layer, rope);
-  if (b.kv_checked)
-    launch_pdl(attention_pv_kernel<false>, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
-  else
-    launch_pdl(attention_pv_kernel<true>, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
-  return 2;
 }
 
 }  // namespace pb

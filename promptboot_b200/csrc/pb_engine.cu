@@ -13,6 +13,7 @@
 #include "pb_kernels.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <initializer_list>
 #include <vector>
 
@@ -91,31 +92,32 @@ cudaError_t dalloc(T** p, size_t count) {
   return cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(count, 1) * sizeof(T));
 }
 
-__global__ void advance_kernel(const pb::SamplerRow* sampled, uint32_t* tokens, int* positions,
-                               uint32_t* token_log, int n) {
-  pb::pdl_begin();
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  uint32_t id = sampled[i].selected;
-  tokens[i] = id;
-  if (token_log) token_log[i] = id;
-}
-
-__global__ void increment_kernel(int* positions, int n) {
-  pb::pdl_begin();
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) positions[i] += 1;
-}
-
-__global__ void record_sampler_status(const pb::SamplerRow* sampled, unsigned long long* status_log,
-                                      int n) {
+// The generate loop's per-step bookkeeping kernels.  A row's step index
+// within the current chunk is positions[i] - base[i] (base = its position when
+// the chunk began), so every step enqueues the same launches with the same
+// arguments and one captured CUDA graph replays any step.
+__global__ void take_sample_kernel(const pb::SamplerRow* sampled, uint32_t* tokens,
+                                   const int* positions, const int* base,
+                                   unsigned long long* status_log, uint32_t* token_log, int n) {
   pb::pdl_begin();
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const pb::SamplerRow r = sampled[i];
-  status_log[i] = r.status ? (((unsigned long long)r.status << 56) |
-                              ((unsigned long long)r.index << 32) | r.value)
-                           : pb::kNoError;
+  const size_t at = (size_t)(positions[i] - base[i]) * n + i;
+  tokens[i] = r.selected;
+  token_log[at] = r.selected;
+  status_log[at] = r.status ? (((unsigned long long)r.status << 56) |
+                               ((unsigned long long)r.index << 32) | r.value)
+                            : pb::kNoError;
+}
+
+__global__ void finish_step_kernel(int* positions, const int* base, const unsigned long long* err,
+                                   unsigned long long* err_log, int n) {
+  pb::pdl_begin();
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  err_log[(size_t)(positions[i] - base[i]) * n + i] = err[i];
+  positions[i] += 1;
 }
 
 }  // namespace
@@ -155,6 +157,32 @@ struct pb_engine {
   uint32_t* d_token_log = nullptr;              // [kErrSteps][max_seqs]
   unsigned int* d_tc_status = nullptr;          // tensor-core pipeline timeout flag
   unsigned int* h_tc_status = nullptr;
+  int* d_base = nullptr;                        // [max_seqs] positions at the chunk's start
+  unsigned long long* d_err_cur = nullptr;      // [max_seqs] this step's stage errors
+
+  // CUDA graphs of whole steps.  A step's launches depend on the host only
+  // through the key below (the softmax span is rounded up to 64 positions for
+  // this: wider shared-memory tiles, the same results), so a step whose key was
+  // seen before replays its graph.  The first occurrence of a key runs
+  // directly (kernel attributes are set there), the second is captured.
+  struct GraphKey {
+    uint32_t rows;
+    int span;
+    int kind;  // 0 decode forward, 1 generate step, 2 generate step + greedy
+    bool operator==(const GraphKey& o) const {
+      return rows == o.rows && span == o.span && kind == o.kind;
+    }
+  };
+  struct GraphEntry {
+    GraphKey key;
+    cudaGraphExec_t exec = nullptr;  // null: seen once, not captured yet
+    uint64_t launches = 0;
+    uint64_t used = 0;
+  };
+  std::vector<GraphEntry> graphs;
+  uint64_t graph_clock = 0;
+  bool graphs_enabled = true;
+  static constexpr size_t kMaxGraphs = 16;
 
   // pinned host staging
   int *h_slots = nullptr, *h_positions = nullptr;
@@ -277,6 +305,63 @@ struct pb_engine {
     }
   }
 
+  // Runs `enqueue` (the launches of one step) directly or as a CUDA graph
+  // keyed by `key`; returns false when a CUDA call failed.
+  template <class F>
+  bool run_step(const GraphKey& key, F&& enqueue) {
+    if (!graphs_enabled || prof_mask) {
+      enqueue();
+      return true;
+    }
+    GraphEntry* entry = nullptr;
+    for (GraphEntry& g : graphs)
+      if (g.key == key) entry = &g;
+    if (!entry) {
+      if (graphs.size() == kMaxGraphs) {
+        auto oldest = std::min_element(graphs.begin(), graphs.end(),
+                                       [](const GraphEntry& a, const GraphEntry& b) {
+                                         return a.used < b.used;
+                                       });
+        if (oldest->exec) cudaGraphExecDestroy(oldest->exec);
+        graphs.erase(oldest);
+      }
+      graphs.push_back(GraphEntry{key});
+      graphs.back().used = ++graph_clock;
+      enqueue();  // first occurrence: direct
+      return true;
+    }
+    entry->used = ++graph_clock;
+    if (!entry->exec) {
+      const uint64_t l0 = launches;
+      if (cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        graphs_enabled = false;
+        enqueue();
+        return true;
+      }
+      enqueue();
+      cudaGraph_t graph = nullptr;
+      cudaError_t e = cudaStreamEndCapture(stream, &graph);
+      if (e == cudaSuccess) e = cudaGraphInstantiate(&entry->exec, graph, 0);
+      if (graph) cudaGraphDestroy(graph);
+      entry->launches = launches - l0;
+      launches = l0;
+      if (e != cudaSuccess) {
+        // not capturable here: run without graphs from now on
+        cudaGetLastError();
+        entry->exec = nullptr;
+        graphs_enabled = false;
+        enqueue();
+        return true;
+      }
+    }
+    launches += entry->launches;
+    return cudaGraphLaunch(entry->exec, stream) == cudaSuccess;
+  }
+
+  // The softmax span rounded for the graph key (64 positions; the grouped
+  // path's limit is a multiple of 64, so the choice of path is unchanged).
+  int graph_span(int span) const { return graphs_enabled ? (span + 63) & ~63 : span; }
+
   // Small batches: gate and up rows of one 32-row block per CTA, SwiGLU and the
   // Q8_0 quantization of the products fused into the matvec.
   bool gateup_swiglu(const pb::Batch& b, const uint8_t* gate_w, const uint8_t* up_w,
@@ -359,7 +444,14 @@ struct pb_engine {
     PB_CUDA(cudaMemcpyAsync(d_positions, h_positions, rows * 4, cudaMemcpyHostToDevice, stream));
     max_span = 4;
     for (uint32_t i = 0; i < rows; ++i) max_span = std::max(max_span, (pos[i] + 4) & ~3);
-    enqueue_forward(rows, want_logits, d_err, true, distinct_slots);
+    if (distinct_slots && want_logits) {
+      max_span = graph_span(max_span);
+      if (!run_step(GraphKey{rows, max_span, 0},
+                    [&] { enqueue_forward(rows, true, d_err, true, true); }))
+        PB_CUDA(cudaGetLastError());
+    } else {
+      enqueue_forward(rows, want_logits, d_err, true, distinct_slots);
+    }
     PB_CUDA(cudaGetLastError());
     PB_CUDA(cudaMemcpyAsync(h_err, d_err, rows * 8, cudaMemcpyDeviceToHost, stream));
     PB_CUDA(cudaMemcpyAsync(h_tc_status, d_tc_status, 4, cudaMemcpyDeviceToHost, stream));
@@ -658,6 +750,8 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   chk(dalloc(&e->d_samp_status, S * pb_engine::kErrSteps));
   chk(dalloc(&e->d_token_log, S * pb_engine::kErrSteps));
   chk(dalloc(&e->d_tc_status, 1));
+  chk(dalloc(&e->d_base, S));
+  chk(dalloc(&e->d_err_cur, R));
   chk(cudaMallocHost(&e->h_tc_status, 4));
   chk(cudaMallocHost(&e->h_slots, R * 4));
   chk(cudaMallocHost(&e->h_positions, R * 4));
@@ -666,6 +760,7 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   chk(cudaMallocHost(&e->h_greedy, S * 4));
   chk(cudaMallocHost(&e->h_greedy_bits, S * 4));
   if (c == cudaSuccess) pb::init_kernel_attributes();
+  if (const char* f = std::getenv("PB_GRAPHS")) e->graphs_enabled = std::atoi(f) != 0;
   if (c == cudaSuccess) c = cudaMemsetAsync(e->kv, 0, S * (size_t)max_context * 6144 * 4, e->stream);
   if (c == cudaSuccess) c = cudaMemsetAsync(e->history, 0, S * (size_t)max_context * 4, e->stream);
   if (c == cudaSuccess) c = cudaMemsetAsync(e->d_tc_status, 0, 4, e->stream);
@@ -690,12 +785,14 @@ void pb_engine_destroy(pb_engine* e) {
                  e->logits, e->scores, e->aq, e->ad, e->asum, e->d_slots, e->d_positions,
                  e->d_tokens, e->d_err, e->d_greedy, e->d_greedy_bits, e->d_states,
                  e->d_hist_offset, e->d_hist_len, e->d_sampled, e->d_samp_status,
-                 e->d_token_log, e->d_tc_status, e->aq_tc};
+                 e->d_token_log, e->d_tc_status, e->aq_tc, e->d_base, e->d_err_cur};
   for (void* p : dev) if (p) cudaFree(p);
   void* host[] = {e->h_slots, e->h_positions, e->h_tokens, e->h_err, e->h_greedy, e->h_greedy_bits,
                   e->h_tc_status};
   for (void* p : host) if (p) cudaFreeHost(p);
   for (cudaEvent_t ev : e->prof_events) cudaEventDestroy(ev);
+  for (auto& g : e->graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -1033,26 +1130,32 @@ uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
   const int threads = 128, blocks = (int)((n + threads - 1) / threads);
   for (uint32_t done = 0; done < steps;) {
     const uint32_t chunk = std::min<uint32_t>(pb_engine::kErrSteps, steps - done);
+    // the logs of this chunk are indexed by position - base on the device
+    PB_CUDA(cudaMemcpyAsync(e->d_base, e->d_positions, n * 4, cudaMemcpyDeviceToDevice, e->stream));
     for (uint32_t t = 0; t < chunk; ++t) {
-      // history length == position (every evaluated token is in the history)
-      pb_engine* self = e;
-      self->prof_mark(PB_KC_SAMPLER);
-      pb::launch_sampler(e->logits, 151936, (int)n, 151936, e->history, e->d_hist_offset,
-                         reinterpret_cast<const uint32_t*>(e->d_positions), nullptr, e->d_states,
-                         e->d_sampled, e->stream);
-      self->prof_mark(PB_KC_SAMPLER);
-      pb::launch_pdl(record_sampler_status, blocks, threads, 0, e->stream, e->d_sampled,
-                     e->d_samp_status + (size_t)t * n, (int)n);
-      pb::launch_pdl(advance_kernel, blocks, threads, 0, e->stream, e->d_sampled, e->d_tokens,
-                     e->d_positions, e->d_token_log + (size_t)t * n, (int)n);
-      e->max_span = 4;
+      int span = 4;
       for (uint32_t i = 0; i < n; ++i)
-        e->max_span = std::max(e->max_span,
-                               (int)((e->slots[seqs[i]].position + done + t + 4) & ~3u));
+        span = std::max(span, (int)((e->slots[seqs[i]].position + done + t + 4) & ~3u));
       // Only the last step's greedy id is published (InferenceStep::selected).
-      e->enqueue_forward(n, true, e->d_err + (size_t)t * n, done + t + 1 == steps);
-      pb::launch_pdl(increment_kernel, blocks, threads, 0, e->stream, e->d_positions, (int)n);
-      e->launches += 4;
+      const bool greedy = done + t + 1 == steps;
+      e->max_span = e->graph_span(span);
+      auto one_step = [&] {
+        // history length == position (every evaluated token is in the history)
+        e->prof_mark(PB_KC_SAMPLER);
+        pb::launch_sampler(e->logits, 151936, (int)n, 151936, e->history, e->d_hist_offset,
+                           reinterpret_cast<const uint32_t*>(e->d_positions), nullptr, e->d_states,
+                           e->d_sampled, e->stream);
+        e->prof_mark(PB_KC_SAMPLER);
+        pb::launch_pdl(take_sample_kernel, blocks, threads, 0, e->stream, e->d_sampled,
+                       e->d_tokens, e->d_positions, e->d_base, e->d_samp_status, e->d_token_log,
+                       (int)n);
+        e->enqueue_forward(n, true, e->d_err_cur, greedy);
+        pb::launch_pdl(finish_step_kernel, blocks, threads, 0, e->stream, e->d_positions, e->d_base,
+                       e->d_err_cur, e->d_err, (int)n);
+        e->launches += 3;
+      };
+      if (!e->run_step(pb_engine::GraphKey{n, e->max_span, greedy ? 2 : 1}, one_step))
+        PB_CUDA(cudaGetLastError());
     }
     PB_CUDA(cudaGetLastError());
     std::vector<unsigned long long> serr((size_t)chunk * n);

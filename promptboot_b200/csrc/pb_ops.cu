@@ -534,7 +534,9 @@ uint32_t pb_expf_device(const uint32_t* x, uint64_t n, uint32_t* y, void* stream
 uint32_t pb_attention_device(const float* q, const float* kv, uint32_t capacity, uint32_t layer,
                              const uint32_t* positions_host, uint32_t rows, uint32_t span,
                              float* out, float* scores, void* stream) {
-  if (rows == 0 || capacity == 0 || (capacity & 3) || layer >= 24 || (span & 3)) return PB_CAPACITY;
+  if (rows == 0 || capacity == 0 || (capacity & 3) || capacity > PB_CONTEXT_LIMIT || layer >= 24 ||
+      (span & 3) || span > PB_CONTEXT_LIMIT)
+    return PB_CAPACITY;
   uint32_t span_max = span;
   for (uint32_t r = 0; r < rows; ++r) {
     if (positions_host[r] >= capacity) return PB_CAPACITY;
