@@ -331,8 +331,10 @@ def run_config3(args, world, rank, local, img):
                 barrier(world)
                 torch.cuda.synchronize()
                 l0 = lib.pb_engine_launch_count(eng._h)
+                torch.cuda.nvtx.range_push("pb_timed")  # ncu --nvtx --nvtx-include pb_timed/
                 with Events(stream) as ev:
                     st, _, errs = eng.generate(seqs, states, 1, want_tokens=False)
+                torch.cuda.nvtx.range_pop()
                 ms = ev.ms()
                 torch.cuda.synchronize()
                 barrier(world)
