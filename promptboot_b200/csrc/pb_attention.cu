@@ -9,27 +9,27 @@
 //   sum = sum over 4-groups IN ORDER of f64(fl(fl(e0+e1) + fl(e2+e3)))   one lane per head
 //   prob = fl(e * f32(1.0 / sum))
 //   out[h][c] = f32(sum_p f64(fl(prob[h][p] * v[p][c])))              p in order
-// Two launches, both 224 threads = one warp per query head of a KV head, so q
-// and the probabilities are warp broadcasts and the softmax needs no block
-// barrier:
-//  * attention_scores_kernel: one CTA per (sequence, KV head, 64-position
-//    chunk), so thousands of small CTAs keep every SM busy while K streams in.
-//    K arrives in the reference's 4-position tiles ([component][4 positions],
-//    1 KB) and is copied untransposed by cp.async into tiles padded to 260
-//    words: lane (tile, pair) reads positions 4 tile + 2 pair + {0, 1} of one
-//    component with one 8-byte load (two independent f64 chains per lane), and
-//    a half-warp covers all 32 banks once.  Scores go to the global score
-//    scratch (L2-resident).  With the RoPE table given, every CTA rotates q for
-//    its 7 heads and the CTA of the last chunk also rotates k and writes this
-//    step's K and V (decode steps, where no two rows share a slot).
-//  * attention_pv_kernel: one CTA per (sequence, KV head); the softmax of each
-//    head runs in its warp from the global scores, then V streams through two
+// Every launch serves the 7 query heads of one KV head together.
+//  * attention_scores4_kernel: one CTA per (sequence, KV head, 128-position
+//    chunk), 224 threads = one warp per query head, so thousands of small CTAs
+//    keep every SM busy while K streams in.  K arrives in the reference's
+//    4-position tiles ([component][4 positions], 1 KB) and is copied
+//    untransposed by cp.async into tiles padded to 260 words; lane l of a warp
+//    takes tile l, one 16-byte shared load per component serving 4 products,
+//    and keeps 4 f64 chains (two converting their products on the XU pipe, two
+//    summing integer-built images, scaled_image).  Scores go to the global
+//    score scratch (L2-resident).  With the RoPE table given, every CTA
+//    rotates q for its 7 heads and the CTA of the last chunk also rotates k and
+//    writes this step's K and V (decode steps, where no two rows share a slot).
+//  * up to kAttnMaxPositions, attention_pv_kernel: one CTA per (sequence, KV
+//    head), one warp per query head; the softmax of each head runs in its warp
+//    from the scores copied into shared memory, then V streams through two
 //    64-row buffers while every lane keeps two f64 chains (components 2 lane
 //    and 2 lane + 1, one 8-byte load per position, positions in order); the
 //    second chain adds integer-built f64 images of its products instead of
 //    converting them (scaled_product).
-// The probabilities live in shared memory, so this path serves contexts up to
-// kAttnMaxPositions; longer ones use the long-context launches below.
+//  * beyond that, the probabilities stay in the global scratch: the softmax
+//    launch and the one-chain-per-thread PV launch below.
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
 #include "pb_quant.cuh"
@@ -80,105 +80,6 @@ struct PvSmem {
   static constexpr int kVBuf = kChunk * 64;  // V rows
   static size_t bytes(int span_cap) { return (size_t)(2 * kVBuf + kHeadsPerKv * span_cap) * 4; }
 };
-
-__global__ void __launch_bounds__(kThreads, 8)
-attention_scores_kernel(Batch b, int layer, const float* rope) {
-  pdl_begin();
-  __shared__ __align__(16) float qs[kHeadsPerKv * 64];
-  __shared__ __align__(16) float ks[(kChunk / 4) * kTilePitch];
-
-  const int t = blockIdx.x, row = blockIdx.y >> 1, kh = blockIdx.y & 1;
-  const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
-  const int positions = b.positions[row] + 1;
-  if (t * kChunk >= positions) return;
-  const bool last = (t + 1) * kChunk >= positions;
-  const size_t cap = b.capacity;
-  const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
-  const float* kbase = kv + (size_t)layer * 4 * cap * 64 + (size_t)kh * (cap / 4) * 256;
-
-  const float* qg = b.q + (size_t)row * kHidden + kh * kHeadsPerKv * 64;
-  if (rope) {
-    // RoPE and the KV write of this step's position (fp32_sse2.rs:1413-1428,
-    // inference.rs:1809-1887), for this CTA's 7 query heads and its KV head:
-    // lane `pair` of warp h rotates (pair, pair + 32) of head 7 kh + h; in the
-    // last chunk's CTA warp 0 also rotates K head kh and writes it, warps 1-2
-    // write V head kh, and the stage checks are recorded once.
-    const int position = positions - 1;
-    const uint32_t ord = (uint32_t)layer + 1;
-    const float* table = rope + (size_t)position * 64;
-    const float c = table[lane * 2], sn = table[lane * 2 + 1];
-    {
-      const float left = qg[h * 64 + lane], right = qg[h * 64 + lane + 32];
-      const float l2 = __fsub_rn(__fmul_rn(left, c), __fmul_rn(right, sn));
-      const float r2 = __fadd_rn(__fmul_rn(left, sn), __fmul_rn(right, c));
-      qs[h * 64 + lane] = l2;
-      qs[h * 64 + lane + 32] = r2;
-      if (last) {
-        const int qi = (kh * kHeadsPerKv + h) * 64 + lane;
-        check_finite(l2, &b.err[row], ord, D_ROPE, 0, qi);
-        check_finite(r2, &b.err[row], ord, D_ROPE, 0, qi + 32);
-      }
-    }
-    if (last) {
-      float* kvs = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
-      if (h == 0) {
-        const float* kg = b.k + (size_t)row * 128 + kh * 64;
-        const float left = kg[lane], right = kg[lane + 32];
-        const float l2 = __fsub_rn(__fmul_rn(left, c), __fmul_rn(right, sn));
-        const float r2 = __fadd_rn(__fmul_rn(left, sn), __fmul_rn(right, c));
-        check_finite(l2, &b.err[row], ord, D_ROPE, 1, kh * 64 + lane);
-        check_finite(r2, &b.err[row], ord, D_ROPE, 1, kh * 64 + lane + 32);
-        check_finite(l2, &b.err[row], ord, D_KV, 0, kh * 64 + lane);
-        check_finite(r2, &b.err[row], ord, D_KV, 0, kh * 64 + lane + 32);
-        kvs[kv_key_word(cap, layer, kh, position, lane)] = l2;
-        kvs[kv_key_word(cap, layer, kh, position, lane + 32)] = r2;
-      } else if (h <= 2) {
-        const int cc = (h - 1) * 32 + lane;
-        kvs[kv_value_word(cap, layer, kh, position, cc)] = b.v[(size_t)row * 128 + kh * 64 + cc];
-      }
-      __threadfence();  // the cp.async reads below go through L2
-    }
-  } else {
-    qs[tid] = qg[tid];
-    qs[tid + kThreads] = qg[tid + kThreads];
-  }
-  __syncthreads();
-
-  // Chunk t = K tiles 16t .. 16t + 15, each 1 KB contiguous in the cache.
-  {
-    const int ntiles = (positions + 3) >> 2;
-    const int tiles = min(kChunk / 4, ntiles - t * (kChunk / 4));
-    const float* src = kbase + (size_t)t * (kChunk / 4) * 256;
-    for (int i = tid; i < tiles * 64; i += kThreads)
-      cp_async16(ks + (i >> 6) * kTilePitch + (i & 63) * 4, src + i * 4);
-    cp_commit();
-    cp_wait0();
-  }
-  __syncthreads();
-
-  // lane (tile, pair) -> positions 4 tile + 2 pair + {0, 1} of the chunk
-  const int tile = lane >> 1, pair = lane & 1;
-  const float* qh = qs + h * 64;
-  const float* kt = ks + tile * kTilePitch + 2 * pair;
-  const int p = t * kChunk + 4 * tile + 2 * pair;
-  if (p < positions) {
-    double d0 = 0.0, d1 = 0.0;
-#pragma unroll 4
-    for (int c = 0; c < 64; c += 4) {
-      const float4 q4 = *reinterpret_cast<const float4*>(qh + c);
-      const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 k2 = *reinterpret_cast<const float2*>(kt + (c + j) * 4);
-        d0 += (double)__fmul_rn(qv[j], k2.x);
-        d1 += (double)__fmul_rn(qv[j], k2.y);
-      }
-    }
-    float* out = b.scores + ((size_t)row * kQHeads + kh * kHeadsPerKv + h) * b.score_stride;
-    out[p] = __fmul_rn((float)d0, 0.125f);
-    if (p + 1 < positions) out[p + 1] = __fmul_rn((float)d1, 0.125f);
-  }
-}
 
 template <bool kCheckV>
 __global__ void __launch_bounds__(kThreads, 4)
@@ -307,7 +208,7 @@ attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
 // ------------------------------------------------------------ long contexts
 //
 // Beyond kAttnMaxPositions the probabilities no longer fit in shared memory.
-// The scores come from attention_scores_kernel as above; then
+// The scores come from attention_scores4_kernel as above; then
 //  * attention_softmax_long_kernel, one CTA per (sequence, query head): the
 //    maximum, e = expf4(s - max) with the span padded by zeros, the 4-lane
 //    group terms g = fl(fl(e0+e1) + fl(e2+e3)), their f64 sum, and the
@@ -318,14 +219,8 @@ attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
 //    exactly representable and all orders give the exact total; otherwise one
 //    thread repeats the serial sum in group order over the terms kept in
 //    shared memory.
-//  * attention_pv_long_kernel<G>, one CTA per (sequence, KV head, one of G
-//    component groups): a thread owns the two f64 chains of components
-//    (2 c, 2 c + 1) of one head over all positions in order, V rows of the
-//    group and the 7 heads' probabilities streaming through shared memory, so
-//    every V word is read once per KV head and the 7 x 64 chains of a KV head
-//    run on G SMs.  Each chain is one dependent f64 add per position (8.2
-//    cycles measured on B200): at 31k positions that latency, not HBM, bounds
-//    the launch.
+//  * attention_pv_chains_kernel<G> (below): one f64 chain per thread over all
+//    positions, every V word read once per KV head.
 
 constexpr int kLongThreads = 256;
 constexpr int kLongMaxGroups = kContextLimit / 4;  // spans of at most 32768 positions
@@ -426,50 +321,53 @@ attention_softmax_long_kernel(Batch b) {
   }
 }
 
-// G component groups of 64 / G components per CTA; a thread owns the two
-// chains of components (2 c, 2 c + 1) of one head, the first converting its
-// products on the XU pipe, the second summing integer-built images
-// (scaled_product), like attention_pv_kernel.  kLongStages chunks of
-// kLongChunk positions are in flight (V rows of the group and the 7 heads'
-// probabilities, cp.async into shared memory).
-constexpr int kLongChunk = 128;
-constexpr int kLongStages = 4;
-
+// The PV chains over probabilities in the global score scratch.  A CTA serves
+// one (sequence, KV head, one of G component groups); thread (head h,
+// component c) owns ONE f64 chain over all positions in order, converting its
+// products on the XU pipe.  Each position then costs a thread about five
+// instructions (a broadcast probability load, one V load, the product, its
+// conversion and the dependent add), so the launch runs at the chain latency
+// (one dependent f64 add per position, 8.2 cycles on B200) instead of a
+// warp's issue rate; the 448 chains of a KV head spread over G CTAs keep the
+// conversions of one SM below that latency.  Chunks of V rows of the group and
+// the 7 heads' probabilities stream through kStages cp.async buffers.
 template <int G>
-struct PvLong {
-  static constexpr int kComps = 64 / G;                           // components per CTA
-  static constexpr int kPairs = kComps / 2;                       // threads per head
-  static constexpr int kWorkers = kHeadsPerKv * kPairs;
+struct PvChains {
+  static constexpr int kComps = 64 / G;                            // components per CTA
+  static constexpr int kWorkers = kHeadsPerKv * kComps;            // one chain each
   static constexpr int kThreads = (kWorkers + 31) / 32 * 32;
-  static constexpr int kVWords = kLongChunk * kComps;              // V rows of one chunk
-  static constexpr int kPWords = kHeadsPerKv * kLongChunk;         // probabilities of one chunk
+  static constexpr int kChunk = 128;                               // positions per stage
+  static constexpr int kStages = 4;
+  static constexpr int kVWords = kChunk * kComps;
+  static constexpr int kPWords = kHeadsPerKv * kChunk;
   static constexpr int kStage = kVWords + kPWords;
-  static constexpr size_t kBytes = (size_t)kLongStages * kStage * 4;
+  static constexpr size_t kBytes = (size_t)kStages * kStage * 4;
+  static_assert(kComps % 4 == 0, "16-byte V pieces");
 };
 
-template <int G, bool kCheckV>
-__global__ void __launch_bounds__(PvLong<G>::kThreads)
-attention_pv_long_kernel(Batch b, int layer) {
-  using C = PvLong<G>;
+template <int G>
+__global__ void __launch_bounds__(PvChains<G>::kThreads)
+attention_pv_chains_kernel(Batch b, int layer) {
+  using C = PvChains<G>;
   pdl_begin();
   extern __shared__ __align__(16) float sm[];
   const int row = blockIdx.x >> 1, kh = blockIdx.x & 1, grp = blockIdx.y;
   const int tid = threadIdx.x;
-  const int h = tid / C::kPairs, c2 = tid % C::kPairs;
+  const int h = tid / C::kComps, cc = tid % C::kComps;
   const bool active = tid < C::kWorkers;
-  const int comp = grp * C::kComps + 2 * c2;  // this thread's first component
+  const int comp = grp * C::kComps + cc;
   const int positions = b.positions[row] + 1;
   const size_t cap = b.capacity;
   const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
   const float* vbase = kv + (size_t)layer * 4 * cap * 64 + 2 * cap * 64 + (size_t)kh * cap * 64;
   const float* probs = b.scores + ((size_t)row * kQHeads + kh * kHeadsPerKv) * b.score_stride;
-  const int nchunks = (positions + kLongChunk - 1) / kLongChunk;
+  const int nchunks = (positions + C::kChunk - 1) / C::kChunk;
 
   auto load = [&](int t) {
     if (t < nchunks) {
-      float* stage = sm + (t % kLongStages) * C::kStage;
-      const int p0 = t * kLongChunk;
-      const int rows_here = min(kLongChunk, positions - p0);
+      float* stage = sm + (t % C::kStages) * C::kStage;
+      const int p0 = t * C::kChunk;
+      const int rows_here = min(C::kChunk, positions - p0);
       constexpr int kPieces = C::kComps / 4;
       for (int i = tid; i < rows_here * kPieces; i += C::kThreads) {
         const int r = i / kPieces, piece = i % kPieces;
@@ -482,80 +380,201 @@ attention_pv_long_kernel(Batch b, int layer) {
       float* pst = stage + C::kVWords;
       for (int i = tid; i < kHeadsPerKv * quads; i += C::kThreads) {
         const int hh = i / quads, q = i % quads;
-        cp_async16(pst + hh * kLongChunk + 4 * q, probs + (size_t)hh * b.score_stride + p0 + 4 * q);
+        cp_async16(pst + hh * C::kChunk + 4 * q, probs + (size_t)hh * b.score_stride + p0 + 4 * q);
       }
     }
     cp_commit();  // one group per chunk slot, empty past the end
   };
 #pragma unroll
-  for (int t = 0; t < kLongStages - 1; ++t) load(t);
+  for (int t = 0; t < C::kStages - 1; ++t) load(t);
 
-  double acc0 = 0.0, acc1 = 0.0;
-  float vchk = 0.0f;
+  double acc = 0.0;
   for (int t = 0; t < nchunks; ++t) {
-    load(t + kLongStages - 1);
-    asm volatile("cp.async.wait_group %0;" ::"n"(kLongStages - 1) : "memory");
+    load(t + C::kStages - 1);
+    asm volatile("cp.async.wait_group %0;" ::"n"(C::kStages - 1) : "memory");
     __syncthreads();
-    const float* stage = sm + (t % kLongStages) * C::kStage;
-    const float* vt = stage + 2 * c2;  // this thread's component pair in each V row
-    const float* pr = stage + C::kVWords + h * kLongChunk;
-    const int rows_here = min(kLongChunk, positions - t * kLongChunk);
+    const float* stage = sm + (t % C::kStages) * C::kStage;
+    const float* vt = stage + cc;
+    const float* pr = stage + C::kVWords + h * C::kChunk;
+    const int rows_here = min(C::kChunk, positions - t * C::kChunk);
     if (active) {
       int i = 0;
       for (; i + 8 <= rows_here; i += 8) {
         const float4 pa = *reinterpret_cast<const float4*>(pr + i);
         const float4 pb = *reinterpret_cast<const float4*>(pr + i + 4);
         const float pv[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-        float2 v[8];
+        float v[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const float2*>(vt + (i + j) * C::kComps);
+        for (int k = 0; k < 8; ++k) v[k] = vt[(i + k) * C::kComps];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          acc0 += (double)__fmul_rn(pv[j], v[j].x);
-          acc1 += scaled_product(pv[j], v[j].y);
-          if (kCheckV) vchk = __fmaf_rn(v[j].y, 0.0f, vchk);
-        }
+        for (int k = 0; k < 8; ++k) acc += (double)__fmul_rn(pv[k], v[k]);
       }
-      for (; i < rows_here; ++i) {
-        const float2 v = *reinterpret_cast<const float2*>(vt + i * C::kComps);
-        acc0 += (double)__fmul_rn(pr[i], v.x);
-        acc1 += scaled_product(pr[i], v.y);
-        if (kCheckV) vchk = __fmaf_rn(v.y, 0.0f, vchk);
-      }
+      for (; i < rows_here; ++i) acc += (double)__fmul_rn(pr[i], vt[i * C::kComps]);
     }
     __syncthreads();  // the slot is refilled by the next iteration's load
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   if (!active) return;
-  const float* hprobs = probs + (size_t)h * b.score_stride;
-  // The scaled chain needs finite products: finite probabilities (a finite
-  // normalizer; a non-finite one shows in every probability word, position
-  // 0's included) and finite V (the v-projection check, or vchk here).
-  const float p0 = hprobs[0];
-  if (fabsf(p0) <= 0x1.fffffep127f && vchk == 0.0f) {
-    acc1 *= 0x1p896;
-  } else {
-    acc1 = 0.0;
-    for (int p = 0; p < positions; ++p)
-      acc1 += (double)__fmul_rn(hprobs[p], vbase[(size_t)p * 64 + comp + 1]);
-  }
-  const float o0 = (float)acc0, o1 = (float)acc1;
+  const float o = (float)acc;
   const int qh_index = kh * kHeadsPerKv + h;
-  *reinterpret_cast<float2*>(b.attn + (size_t)row * kHidden + qh_index * 64 + comp) =
-      make_float2(o0, o1);
-  check_finite(o0, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + comp);
-  check_finite(o1, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + comp + 1);
+  b.attn[(size_t)row * kHidden + qh_index * 64 + comp] = o;
+  check_finite(o, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + comp);
 }
+
+// f64 image of p * 2^-896 for a finite binary32 p (the conversion-free half
+// of scaled_product).
+__device__ __forceinline__ double scaled_image(float p) {
+  double d;
+  asm("{\n\t.reg .b32 hi, lo;\n\t"
+      "shr.s32 hi, %1, 3;\n\t"
+      "and.b32 hi, hi, 0x8FFFFFFF;\n\t"
+      "shl.b32 lo, %1, 29;\n\t"
+      "mov.b64 %0, {lo, hi};\n\t}"
+      : "=d"(d) : "r"(__float_as_uint(p)));
+  return d;
+}
+
+// Scores over chunks of 128 positions: lane l of warp h takes the 4-position K
+// tile l, so one 16-byte shared load serves 4 products, and keeps 4 f64
+// chains: positions 0-1 of the tile convert their products on the XU pipe,
+// positions 2-3 sum integer-built images (scaled_image), redone with
+// conversions when a product of theirs is not finite.  RoPE and this step's
+// K/V write of this step's position when the RoPE table is given.
+constexpr int kChunk4 = 128;
+
+__global__ void __launch_bounds__(kThreads, 6)
+attention_scores4_kernel(Batch b, int layer, const float* rope) {
+  pdl_begin();
+  __shared__ __align__(16) float qs[kHeadsPerKv * 64];
+  extern __shared__ __align__(16) float ks[];  // [32 tiles][kTilePitch]
+
+  const int t = blockIdx.x, row = blockIdx.y >> 1, kh = blockIdx.y & 1;
+  const int tid = threadIdx.x, h = tid >> 5, lane = tid & 31;
+  const int positions = b.positions[row] + 1;
+  if (t * kChunk4 >= positions) return;
+  const bool last = (t + 1) * kChunk4 >= positions;
+  const size_t cap = b.capacity;
+  const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
+  const float* kbase = kv + (size_t)layer * 4 * cap * 64 + (size_t)kh * (cap / 4) * 256;
+
+  const float* qg = b.q + (size_t)row * kHidden + kh * kHeadsPerKv * 64;
+  if (rope) {
+    const int position = positions - 1;
+    const uint32_t ord = (uint32_t)layer + 1;
+    const float* table = rope + (size_t)position * 64;
+    const float c = table[lane * 2], sn = table[lane * 2 + 1];
+    {
+      const float left = qg[h * 64 + lane], right = qg[h * 64 + lane + 32];
+      const float l2 = __fsub_rn(__fmul_rn(left, c), __fmul_rn(right, sn));
+      const float r2 = __fadd_rn(__fmul_rn(left, sn), __fmul_rn(right, c));
+      qs[h * 64 + lane] = l2;
+      qs[h * 64 + lane + 32] = r2;
+      if (last) {
+        const int qi = (kh * kHeadsPerKv + h) * 64 + lane;
+        check_finite(l2, &b.err[row], ord, D_ROPE, 0, qi);
+        check_finite(r2, &b.err[row], ord, D_ROPE, 0, qi + 32);
+      }
+    }
+    if (last) {
+      float* kvs = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
+      if (h == 0) {
+        const float* kg = b.k + (size_t)row * 128 + kh * 64;
+        const float left = kg[lane], right = kg[lane + 32];
+        const float l2 = __fsub_rn(__fmul_rn(left, c), __fmul_rn(right, sn));
+        const float r2 = __fadd_rn(__fmul_rn(left, sn), __fmul_rn(right, c));
+        check_finite(l2, &b.err[row], ord, D_ROPE, 1, kh * 64 + lane);
+        check_finite(r2, &b.err[row], ord, D_ROPE, 1, kh * 64 + lane + 32);
+        check_finite(l2, &b.err[row], ord, D_KV, 0, kh * 64 + lane);
+        check_finite(r2, &b.err[row], ord, D_KV, 0, kh * 64 + lane + 32);
+        kvs[kv_key_word(cap, layer, kh, position, lane)] = l2;
+        kvs[kv_key_word(cap, layer, kh, position, lane + 32)] = r2;
+      } else if (h <= 2) {
+        const int cc = (h - 1) * 32 + lane;
+        kvs[kv_value_word(cap, layer, kh, position, cc)] = b.v[(size_t)row * 128 + kh * 64 + cc];
+      }
+      __threadfence();  // the cp.async reads below go through L2
+    }
+  } else {
+    qs[tid] = qg[tid];
+    qs[tid + kThreads] = qg[tid + kThreads];
+  }
+  __syncthreads();
+
+  // Chunk t = K tiles 32t .. 32t + 31, each 1 KB contiguous in the cache.
+  {
+    const int ntiles = (positions + 3) >> 2;
+    const int tiles = min(kChunk4 / 4, ntiles - t * (kChunk4 / 4));
+    const float* src = kbase + (size_t)t * (kChunk4 / 4) * 256;
+    for (int i = tid; i < tiles * 64; i += kThreads)
+      cp_async16(ks + (i >> 6) * kTilePitch + (i & 63) * 4, src + i * 4);
+    cp_commit();
+    cp_wait0();
+  }
+  __syncthreads();
+
+  const int p = t * kChunk4 + 4 * lane;  // tile `lane`: positions p .. p + 3
+  if (p >= positions) return;
+  const float* qh = qs + h * 64;
+  const float* kt = ks + lane * kTilePitch;
+  double d0 = 0.0, d1 = 0.0, d2 = 0.0, d3 = 0.0;
+  float fchk = 0.0f;
+#pragma unroll 4
+  for (int c = 0; c < 64; c += 4) {
+    const float4 q4 = *reinterpret_cast<const float4*>(qh + c);
+    const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 k4 = *reinterpret_cast<const float4*>(kt + (c + j) * 4);
+      d0 += (double)__fmul_rn(qv[j], k4.x);
+      d1 += (double)__fmul_rn(qv[j], k4.y);
+      const float p2 = __fmul_rn(qv[j], k4.z), p3 = __fmul_rn(qv[j], k4.w);
+      fchk = __fmaf_rn(p2, 0.0f, fchk);
+      fchk = __fmaf_rn(p3, 0.0f, fchk);
+      d2 += scaled_image(p2);
+      d3 += scaled_image(p3);
+    }
+  }
+  if (fchk == 0.0f) {
+    d2 *= 0x1p896;
+    d3 *= 0x1p896;
+  } else {
+    d2 = d3 = 0.0;
+    for (int c = 0; c < 64; ++c) {
+      const float4 k4 = *reinterpret_cast<const float4*>(kt + c * 4);
+      d2 += (double)__fmul_rn(qh[c], k4.z);
+      d3 += (double)__fmul_rn(qh[c], k4.w);
+    }
+  }
+  float* out = b.scores + ((size_t)row * kQHeads + kh * kHeadsPerKv + h) * b.score_stride;
+  *reinterpret_cast<float4*>(out + p) =
+      make_float4(__fmul_rn((float)d0, 0.125f), __fmul_rn((float)d1, 0.125f),
+                  __fmul_rn((float)d2, 0.125f), __fmul_rn((float)d3, 0.125f));
+}
+
+constexpr size_t kScores4Smem = (size_t)(kChunk4 / 4) * kTilePitch * 4;
 
 }  // namespace
 
 int attention_smem_positions() { return kAttnMaxPositions; }
 
-void configure_scores_kernel() {
+template <int G>
+static void launch_pv_chains(const Batch& b, int layer, cudaStream_t s) {
+  using C = PvChains<G>;
   static std::atomic<uint64_t> configured{0};
   if (attribute_needed(configured)) {
-    // 8 score CTAs of 18 KB per SM (the default carveout admits 6)
-    cudaFuncSetAttribute(attention_scores_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(attention_pv_chains_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)C::kBytes);
+    attribute_done(configured);
+  }
+  launch_pdl(attention_pv_chains_kernel<G>, dim3(b.rows * 2, G), C::kThreads, C::kBytes, s, b, layer);
+}
+
+static void configure_scores4() {
+  static std::atomic<uint64_t> configured{0};
+  if (attribute_needed(configured)) {
+    cudaFuncSetAttribute(attention_scores4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kScores4Smem);
+    cudaFuncSetAttribute(attention_scores4_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attribute_done(configured);
   }
 }
@@ -571,9 +590,10 @@ int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quant
                          (int)PvSmem::bytes(kAttnMaxPositions));
     attribute_done(configured);
   }
-  configure_scores_kernel();
-  const int chunks = (span_cap + kChunk - 1) / kChunk;
-  launch_pdl(attention_scores_kernel, dim3(chunks, b.rows * 2), kThreads, 0, s, b, layer, rope);
+  configure_scores4();
+  const int chunks = (span_cap + kChunk4 - 1) / kChunk4;
+  launch_pdl(attention_scores4_kernel, dim3(chunks, b.rows * 2), kThreads, kScores4Smem, s, b, layer,
+             rope);
   if (b.kv_checked)
     launch_pdl(attention_pv_kernel<false>, b.rows * 2, kThreads, bytes, s, b, layer, span_cap, quantize);
   else
@@ -581,44 +601,27 @@ int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quant
   return 2;
 }
 
-// Component groups of the long-context PV launch (PB_ATTN_LONG_GROUPS=2|4|8
+// Component groups of the long-context PV launch (PB_ATTN_LONG_GROUPS=4|8|16
 // in the environment selects one for tuning sweeps; tests cover each).
 int attention_long_groups() {
   if (const char* f = std::getenv("PB_ATTN_LONG_GROUPS")) {
     const int g = std::atoi(f);
-    if (g == 2 || g == 4 || g == 8) return g;
+    if (g == 4 || g == 8 || g == 16) return g;
   }
-  return 4;
-}
-
-template <int G>
-static void launch_pv_long(const Batch& b, int layer, cudaStream_t s) {
-  using C = PvLong<G>;
-  static std::atomic<uint64_t> configured{0};
-  if (attribute_needed(configured)) {
-    cudaFuncSetAttribute(attention_pv_long_kernel<G, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kBytes);
-    cudaFuncSetAttribute(attention_pv_long_kernel<G, true>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kBytes);
-    attribute_done(configured);
-  }
-  const dim3 grid(b.rows * 2, G);
-  if (b.kv_checked)
-    launch_pdl(attention_pv_long_kernel<G, false>, grid, C::kThreads, C::kBytes, s, b, layer);
-  else
-    launch_pdl(attention_pv_long_kernel<G, true>, grid, C::kThreads, C::kBytes, s, b, layer);
+  return 8;
 }
 
 int launch_attention_long(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
                           cudaStream_t s) {
-  configure_scores_kernel();
-  const int chunks = (span_cap + kChunk - 1) / kChunk;
-  launch_pdl(attention_scores_kernel, dim3(chunks, b.rows * 2), kThreads, 0, s, b, layer, rope);
+  configure_scores4();
+  const int chunks = (span_cap + kChunk4 - 1) / kChunk4;
+  launch_pdl(attention_scores4_kernel, dim3(chunks, b.rows * 2), kThreads, kScores4Smem, s, b, layer,
+             rope);
   launch_pdl(attention_softmax_long_kernel, b.rows * kQHeads, kLongThreads, 0, s, b);
   const int groups = attention_long_groups();
-  if (groups == 2) launch_pv_long<2>(b, layer, s);
-  else if (groups == 8) launch_pv_long<8>(b, layer, s);
-  else launch_pv_long<4>(b, layer, s);
+  if (groups == 4) launch_pv_chains<4>(b, layer, s);
+  else if (groups == 16) launch_pv_chains<16>(b, layer, s);
+  else launch_pv_chains<8>(b, layer, s);
   if (quantize) {
     launch_quant(b, b.attn, kHidden, kHidden, s);
     return 4;

@@ -183,6 +183,10 @@ struct pb_engine {
   uint64_t graph_clock = 0;
   bool graphs_enabled = true;
   static constexpr size_t kMaxGraphs = 16;
+  // Graphs pay where the host's launch rate bounds a step: small batches.  A
+  // large batch's step is bound by the GPU, and a capture (~ms) would fall
+  // into whichever step first repeats a key.
+  static constexpr uint32_t kGraphMaxRows = 16;
 
   // pinned host staging
   int *h_slots = nullptr, *h_positions = nullptr;
@@ -309,7 +313,7 @@ struct pb_engine {
   // keyed by `key`; returns false when a CUDA call failed.
   template <class F>
   bool run_step(const GraphKey& key, F&& enqueue) {
-    if (!graphs_enabled || prof_mask) {
+    if (!graphs_enabled || prof_mask || key.rows > kGraphMaxRows) {
       enqueue();
       return true;
     }
@@ -360,7 +364,9 @@ struct pb_engine {
 
   // The softmax span rounded for the graph key (64 positions; the grouped
   // path's limit is a multiple of 64, so the choice of path is unchanged).
-  int graph_span(int span) const { return graphs_enabled ? (span + 63) & ~63 : span; }
+  int graph_span(int span, uint32_t rows) const {
+    return graphs_enabled && rows <= kGraphMaxRows ? (span + 63) & ~63 : span;
+  }
 
   // Small batches: gate and up rows of one 32-row block per CTA, SwiGLU and the
   // Q8_0 quantization of the products fused into the matvec.
@@ -445,7 +451,7 @@ struct pb_engine {
     max_span = 4;
     for (uint32_t i = 0; i < rows; ++i) max_span = std::max(max_span, (pos[i] + 4) & ~3);
     if (distinct_slots && want_logits) {
-      max_span = graph_span(max_span);
+      max_span = graph_span(max_span, rows);
       if (!run_step(GraphKey{rows, max_span, 0},
                     [&] { enqueue_forward(rows, true, d_err, true, true); }))
         PB_CUDA(cudaGetLastError());
@@ -1138,7 +1144,7 @@ uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
         span = std::max(span, (int)((e->slots[seqs[i]].position + done + t + 4) & ~3u));
       // Only the last step's greedy id is published (InferenceStep::selected).
       const bool greedy = done + t + 1 == steps;
-      e->max_span = e->graph_span(span);
+      e->max_span = e->graph_span(span, n);
       auto one_step = [&] {
         // history length == position (every evaluated token is in the history)
         e->prof_mark(PB_KC_SAMPLER);

@@ -10,6 +10,7 @@
 #include "pb_quant.cuh"
 
 #include <cstdio>
+#include <cstdlib>
 
 namespace pb {
 
@@ -365,7 +366,9 @@ void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s
 
 int launch_attention(const Batch& b, int layer, int max_span, bool quantize, const float* rope,
                      cudaStream_t s) {
-  if (max_span <= kAttnMaxPositions)
+  const char* f = std::getenv("PB_ATTN_SPLIT");
+  const bool split = f && std::atoi(f) != 0;
+  if (max_span <= kAttnMaxPositions && !split)
     return launch_attention_grouped(b, layer, (max_span + 3) & ~3, quantize, rope, s);
   return launch_attention_long(b, layer, (max_span + 3) & ~3, quantize, rope, s);
 }

@@ -275,12 +275,12 @@ def test_attention_extreme_magnitudes_match_oracle(case):
         assert _same_bits_or_nan(got[r], ref), (case, r, positions[r])
 
 
-@pytest.mark.parametrize("groups", ["2", "4", "8"])
+@pytest.mark.parametrize("groups", ["4", "8", "16"])
 @pytest.mark.parametrize("case", ["random", "wide_scores", "overflowing_products", "inf_value",
                                   "nan_key", "tiny_values", "wide_values"])
 def test_attention_long_context_extremes_match_oracle(monkeypatch, case, groups):
     """The long-context path (probabilities in the global scratch, the softmax
-    sum as an exact tree or its serial fallback, PV chains split into 2, 4 or 8
+    sum as an exact tree or its serial fallback, PV chains split into 4, 8 or 16
     component groups) against the oracle, probabilities included: random K/V
     (the tree sum holds), scores spread over ~200 units (subnormal
     exponentials: the serial fallback), and the non-finite and extreme cases of
@@ -330,6 +330,52 @@ def test_attention_long_context_extremes_match_oracle(monkeypatch, case, groups)
                                       span)
         assert _same_bits_or_nan(got[r], ref), (case, r, positions[r])
         assert _same_bits_or_nan(got_p[r, 13, :span], ref_p[:span]), (case, r)
+
+
+@pytest.mark.parametrize("case", ["random", "wide_values", "inf_value", "nan_key", "wide_scores"])
+def test_attention_split_path_many_rows_matches_oracle(monkeypatch, case):
+    """The long-context launches (scores, global softmax, one-chain PV) forced
+    for every span at 64 rows, spans from 1 position past 2,048, with the
+    extreme cases that force every fallback (non-finite products in the
+    integer-built score chains, the serial softmax sum)."""
+    monkeypatch.setenv("PB_ATTN_SPLIT", "1")
+    lib = _lib.load()
+    cap, layer, rows = 2304, 0, 64
+    rng = np.random.default_rng(sum(map(ord, case)))
+    positions = [int(x) for x in rng.integers(0, 2300, rows)]
+    positions[:6] = [0, 1, 2, 3, 127, 2299]
+    slot = 24 * 4 * cap * 64
+    kv_d = torch.zeros(rows * slot, dtype=torch.float32, device="cuda")
+    regions = []
+    q = rng.standard_normal((rows, 896)).astype(np.float32)
+    for r in range(rows):
+        kvr = rng.standard_normal(4 * cap * 64).astype(np.float32)
+        p = positions[r] // 2
+        if case == "wide_values":
+            e = rng.integers(-140, 31, 2 * cap * 64)
+            kvr[2 * cap * 64:] = (kvr[2 * cap * 64:] * np.exp2(e)).astype(np.float32)
+        elif case == "inf_value":
+            kvr[oracle.kv_word(cap, 0, 1, p, r & 1, 17)] = np.float32(np.inf)
+        elif case == "nan_key":
+            kvr[oracle.kv_word(cap, 0, 0, p, r & 1, 63)] = np.float32(np.nan)
+        elif case == "wide_scores":
+            q[r] *= np.float32(3.0)
+            for c in range(64):
+                kvr[oracle.kv_word(cap, 0, 0, p, r & 1, c)] *= np.float32(40.0)
+        regions.append(kvr)
+        kv_d[r * slot:r * slot + kvr.size] = torch.from_numpy(kvr).to("cuda")
+    out = torch.zeros((rows, 896), dtype=torch.float32, device="cuda")
+    pos = np.array(positions, dtype=np.uint32)
+    assert lib.pb_attention_device(ptr(dev(q)), ptr(kv_d), cap, layer,
+                                   pos.ctypes.data_as(ctypes.c_void_p), rows, 0, ptr(out), None,
+                                   None) == 0
+    sync()
+    got = host(out)
+    full = np.zeros(slot, dtype=np.float32)
+    for r in range(rows):
+        full[:regions[r].size] = regions[r]
+        ref, _ = oracle.attention(q[r], full, cap, layer, positions[r], (positions[r] + 4) & ~3)
+        assert _same_bits_or_nan(got[r], ref), (case, r, positions[r])
 
 
 def _q4_weights(rng, rows, cols):
