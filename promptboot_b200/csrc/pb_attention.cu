@@ -76,6 +76,19 @@ __device__ __forceinline__ double scaled_product(float a, float b) {
   return d;
 }
 
+// f64 image of p * 2^-896 for a finite binary32 p (the conversion-free half
+// of scaled_product).
+__device__ __forceinline__ double scaled_image(float p) {
+  double d;
+  asm("{\n\t.reg .b32 hi, lo;\n\t"
+      "shr.s32 hi, %1, 3;\n\t"
+      "and.b32 hi, hi, 0x8FFFFFFF;\n\t"
+      "shl.b32 lo, %1, 29;\n\t"
+      "mov.b64 %0, {lo, hi};\n\t}"
+      : "=d"(d) : "r"(__float_as_uint(p)));
+  return d;
+}
+
 struct PvSmem {
   static constexpr int kVBuf = kChunk * 64;  // V rows
   static size_t bytes(int span_cap) { return (size_t)(2 * kVBuf + kHeadsPerKv * span_cap) * 4; }
@@ -159,12 +172,20 @@ attention_pv_kernel(Batch b, int layer, int span_cap, bool quantize) {
     for (; i + 4 <= rows_here; i += 4) {
       const float4 p4 = *reinterpret_cast<const float4*>(pr + i);
       const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+      // the products and their f64 images first, then the two dependent add
+      // chains
+      double t0[4], t1[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 v2 = *reinterpret_cast<const float2*>(vt + (i + j) * 64);
-        acc0 += (double)__fmul_rn(pv[j], v2.x);
-        acc1 += scaled_product(pv[j], v2.y);
+        t0[j] = (double)__fmul_rn(pv[j], v2.x);
+        t1[j] = scaled_product(pv[j], v2.y);
         if (kCheckV) vchk = __fmaf_rn(v2.y, 0.0f, vchk);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc0 += t0[j];
+        acc1 += t1[j];
       }
     }
     for (; i < rows_here; ++i) {
@@ -323,14 +344,17 @@ attention_softmax_long_kernel(Batch b) {
 
 // The PV chains over probabilities in the global score scratch.  A CTA serves
 // one (sequence, KV head, one of G component groups); thread (head h,
-// component c) owns ONE f64 chain over all positions in order, converting its
-// products on the XU pipe.  Each position then costs a thread about five
-// instructions (a broadcast probability load, one V load, the product, its
-// conversion and the dependent add), so the launch runs at the chain latency
-// (one dependent f64 add per position, 8.2 cycles on B200) instead of a
-// warp's issue rate; the 448 chains of a KV head spread over G CTAs keep the
-// conversions of one SM below that latency.  Chunks of V rows of the group and
-// the 7 heads' probabilities stream through kStages cp.async buffers.
+// component c) owns ONE f64 chain over all positions in order.  The chain sums
+// integer-built images of its products (scaled_image; converting them on the
+// XU pipe measured no faster), with the exact conversion fallback of
+// attention_pv_kernel when a probability or a V word is not finite.  V rows of
+// the group (transposed in shared memory) and the 7 heads' probabilities
+// stream through kStages cp.async buffers.  Each position costs a thread about
+// nine instructions, and one warp alone on its scheduler issues them at ~2.5
+// cycles each: ~22 cycles per position per chain, against the 8.2-cycle
+// latency of the dependent f64 add that bounds any order-preserving chain.
+// More CTAs (G 8, 16) do not help: the time is one thread's chain, and the
+// 7 x 64 chains of a KV head run in parallel already.
 template <int G>
 struct PvChains {
   static constexpr int kComps = 64 / G;                            // components per CTA
@@ -338,14 +362,22 @@ struct PvChains {
   static constexpr int kThreads = (kWorkers + 31) / 32 * 32;
   static constexpr int kChunk = 128;                               // positions per stage
   static constexpr int kStages = 4;
-  static constexpr int kVWords = kChunk * kComps;
+  // V of a stage is component-major, [component][kVPitch positions], so a
+  // thread reads four positions of its component with one 16-byte load; the
+  // pitch's 4 extra words put the 8 components of a quarter-warp on distinct
+  // banks.
+  static constexpr int kVPitch = kChunk + 4;
+  static constexpr int kVWords = kComps * kVPitch;
   static constexpr int kPWords = kHeadsPerKv * kChunk;
   static constexpr int kStage = kVWords + kPWords;
   static constexpr size_t kBytes = (size_t)kStages * kStage * 4;
-  static_assert(kComps % 4 == 0, "16-byte V pieces");
 };
 
-template <int G>
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+template <int G, bool kScaled, bool kCheckV>
 __global__ void __launch_bounds__(PvChains<G>::kThreads)
 attention_pv_chains_kernel(Batch b, int layer) {
   using C = PvChains<G>;
@@ -368,11 +400,11 @@ attention_pv_chains_kernel(Batch b, int layer) {
       float* stage = sm + (t % C::kStages) * C::kStage;
       const int p0 = t * C::kChunk;
       const int rows_here = min(C::kChunk, positions - p0);
-      constexpr int kPieces = C::kComps / 4;
-      for (int i = tid; i < rows_here * kPieces; i += C::kThreads) {
-        const int r = i / kPieces, piece = i % kPieces;
-        cp_async16(stage + r * C::kComps + piece * 4,
-                   vbase + (size_t)(p0 + r) * 64 + grp * C::kComps + piece * 4);
+      // V words one by one into the transposed layout (consecutive threads
+      // read consecutive components of a position: 32-byte global segments)
+      for (int i = tid; i < rows_here * C::kComps; i += C::kThreads) {
+        const int r = i / C::kComps, c = i % C::kComps;
+        cp_async4(stage + c * C::kVPitch + r, vbase + (size_t)(p0 + r) * 64 + grp * C::kComps + c);
       }
       // probabilities of the 7 heads, rows_here rounded up to 4 (the scratch
       // holds the padded span)
@@ -389,49 +421,83 @@ attention_pv_chains_kernel(Batch b, int layer) {
   for (int t = 0; t < C::kStages - 1; ++t) load(t);
 
   double acc = 0.0;
+  float vchk = 0.0f;
   for (int t = 0; t < nchunks; ++t) {
     load(t + C::kStages - 1);
     asm volatile("cp.async.wait_group %0;" ::"n"(C::kStages - 1) : "memory");
     __syncthreads();
     const float* stage = sm + (t % C::kStages) * C::kStage;
-    const float* vt = stage + cc;
+    const float* vt = stage + cc * C::kVPitch;
     const float* pr = stage + C::kVWords + h * C::kChunk;
     const int rows_here = min(C::kChunk, positions - t * C::kChunk);
     if (active) {
-      int i = 0;
-      for (; i + 8 <= rows_here; i += 8) {
-        const float4 pa = *reinterpret_cast<const float4*>(pr + i);
-        const float4 pb = *reinterpret_cast<const float4*>(pr + i + 4);
-        const float pv[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-        float v[8];
+      // Software pipeline over batches of 8 positions: the raw probabilities
+      // and V words of the next batch are loaded before the current batch, and
+      // each dependent add of the current batch is followed by the product and
+      // conversion of the matching next-batch position, so the add chain never
+      // waits behind a load or a conversion.
+      const int full = rows_here & ~7;
+      if (full > 0) {
+        float pc[8], vc[8];
+        auto fetch = [&](int i, float (&pp)[8], float (&vv)[8]) {
+          const float4 pa = *reinterpret_cast<const float4*>(pr + i);
+          const float4 pb = *reinterpret_cast<const float4*>(pr + i + 4);
+          pp[0] = pa.x; pp[1] = pa.y; pp[2] = pa.z; pp[3] = pa.w;
+          pp[4] = pb.x; pp[5] = pb.y; pp[6] = pb.z; pp[7] = pb.w;
+          const float4 va = *reinterpret_cast<const float4*>(vt + i);
+          const float4 vb = *reinterpret_cast<const float4*>(vt + i + 4);
+          vv[0] = va.x; vv[1] = va.y; vv[2] = va.z; vv[3] = va.w;
+          vv[4] = vb.x; vv[5] = vb.y; vv[6] = vb.z; vv[7] = vb.w;
+        };
+        auto term = [&](float pk, float vk) {
+          if (kCheckV) vchk = __fmaf_rn(vk, 0.0f, vchk);
+          const float prod = __fmul_rn(pk, vk);
+          return kScaled ? scaled_image(prod) : (double)prod;
+        };
+        fetch(0, pc, vc);
+        double cur[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = vt[(i + k) * C::kComps];
+        for (int k = 0; k < 8; ++k) cur[k] = term(pc[k], vc[k]);
+        for (int i = 8; i < full; i += 8) {
+          fetch(i, pc, vc);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc += (double)__fmul_rn(pv[k], v[k]);
+          for (int k = 0; k < 8; ++k) {
+            acc += cur[k];
+            cur[k] = term(pc[k], vc[k]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc += cur[k];
       }
-      for (; i < rows_here; ++i) acc += (double)__fmul_rn(pr[i], vt[i * C::kComps]);
+      for (int i = full; i < rows_here; ++i) {
+        const float v = vt[i];
+        if (kCheckV) vchk = __fmaf_rn(v, 0.0f, vchk);
+        const float prod = __fmul_rn(pr[i], v);
+        acc += kScaled ? scaled_image(prod) : (double)prod;
+      }
     }
     __syncthreads();  // the slot is refilled by the next iteration's load
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   if (!active) return;
+  if (kScaled) {
+    // The scaled images need finite products: finite probabilities (a finite
+    // normalizer; a non-finite one shows in every probability word, position
+    // 0's included) and finite V (the v-projection check, or vchk here);
+    // otherwise the chain is redone with conversions.
+    const float* hprobs = probs + (size_t)h * b.score_stride;
+    if (fabsf(hprobs[0]) <= 0x1.fffffep127f && vchk == 0.0f) {
+      acc *= 0x1p896;
+    } else {
+      acc = 0.0;
+      for (int p = 0; p < positions; ++p)
+        acc += (double)__fmul_rn(hprobs[p], vbase[(size_t)p * 64 + comp]);
+    }
+  }
   const float o = (float)acc;
   const int qh_index = kh * kHeadsPerKv + h;
   b.attn[(size_t)row * kHidden + qh_index * 64 + comp] = o;
   check_finite(o, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + comp);
-}
-
-// f64 image of p * 2^-896 for a finite binary32 p (the conversion-free half
-// of scaled_product).
-__device__ __forceinline__ double scaled_image(float p) {
-  double d;
-  asm("{\n\t.reg .b32 hi, lo;\n\t"
-      "shr.s32 hi, %1, 3;\n\t"
-      "and.b32 hi, hi, 0x8FFFFFFF;\n\t"
-      "shl.b32 lo, %1, 29;\n\t"
-      "mov.b64 %0, {lo, hi};\n\t}"
-      : "=d"(d) : "r"(__float_as_uint(p)));
-  return d;
 }
 
 // Scores over chunks of 128 positions: lane l of warp h takes the 4-position K
@@ -518,20 +584,29 @@ attention_scores4_kernel(Batch b, int layer, const float* rope) {
   const float* kt = ks + lane * kTilePitch;
   double d0 = 0.0, d1 = 0.0, d2 = 0.0, d3 = 0.0;
   float fchk = 0.0f;
-#pragma unroll 4
+#pragma unroll 2
   for (int c = 0; c < 64; c += 4) {
     const float4 q4 = *reinterpret_cast<const float4*>(qh + c);
     const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+    // the 16 products and their f64 images first, then the four add chains
+    double t[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 k4 = *reinterpret_cast<const float4*>(kt + (c + j) * 4);
-      d0 += (double)__fmul_rn(qv[j], k4.x);
-      d1 += (double)__fmul_rn(qv[j], k4.y);
+      t[j][0] = (double)__fmul_rn(qv[j], k4.x);
+      t[j][1] = (double)__fmul_rn(qv[j], k4.y);
       const float p2 = __fmul_rn(qv[j], k4.z), p3 = __fmul_rn(qv[j], k4.w);
       fchk = __fmaf_rn(p2, 0.0f, fchk);
       fchk = __fmaf_rn(p3, 0.0f, fchk);
-      d2 += scaled_image(p2);
-      d3 += scaled_image(p3);
+      t[j][2] = scaled_image(p2);
+      t[j][3] = scaled_image(p3);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      d0 += t[j][0];
+      d1 += t[j][1];
+      d2 += t[j][2];
+      d3 += t[j][3];
     }
   }
   if (fchk == 0.0f) {
@@ -557,16 +632,23 @@ constexpr size_t kScores4Smem = (size_t)(kChunk4 / 4) * kTilePitch * 4;
 
 int attention_smem_positions() { return kAttnMaxPositions; }
 
-template <int G>
-static void launch_pv_chains(const Batch& b, int layer, cudaStream_t s) {
+template <int G, bool kScaled, bool kCheckV>
+static void launch_pv_chains_as(const Batch& b, int layer, cudaStream_t s) {
   using C = PvChains<G>;
   static std::atomic<uint64_t> configured{0};
   if (attribute_needed(configured)) {
-    cudaFuncSetAttribute(attention_pv_chains_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)C::kBytes);
+    cudaFuncSetAttribute(attention_pv_chains_kernel<G, kScaled, kCheckV>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kBytes);
     attribute_done(configured);
   }
-  launch_pdl(attention_pv_chains_kernel<G>, dim3(b.rows * 2, G), C::kThreads, C::kBytes, s, b, layer);
+  launch_pdl(attention_pv_chains_kernel<G, kScaled, kCheckV>, dim3(b.rows * 2, G), C::kThreads,
+             C::kBytes, s, b, layer);
+}
+
+template <int G>
+static void launch_pv_chains(const Batch& b, int layer, cudaStream_t s) {
+  if (b.kv_checked) launch_pv_chains_as<G, true, false>(b, layer, s);
+  else launch_pv_chains_as<G, true, true>(b, layer, s);
 }
 
 static void configure_scores4() {
@@ -608,7 +690,7 @@ int attention_long_groups() {
     const int g = std::atoi(f);
     if (g == 4 || g == 8 || g == 16) return g;
   }
-  return 8;
+  return 4;
 }
 
 int launch_attention_long(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
