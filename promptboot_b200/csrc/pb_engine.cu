@@ -158,6 +158,7 @@ struct pb_engine {
   unsigned int* d_tc_status = nullptr;          // tensor-core pipeline timeout flag
   unsigned int* h_tc_status = nullptr;
   int* d_base = nullptr;                        // [max_seqs] positions at the chunk's start
+  unsigned long long* d_cand = nullptr;         // split sampler's per-part top-20 lists
   unsigned long long* d_err_cur = nullptr;      // [max_seqs] this step's stage errors
 
   // CUDA graphs of whole steps.  A step's launches depend on the host only
@@ -273,8 +274,20 @@ struct pb_engine {
     int rows;
     pb::Epilogue ep;
   };
+  // The RMSNorm + Q8_0 stage that produces a matvec's input (weight, layer
+  // ordinal, stage domain).
+  struct Norm {
+    const float* w = nullptr;
+    uint32_t ord = 0, domain = 0;
+  };
+  void norm_launch(const pb::Batch& b, const Norm& n) {
+    PB_LAUNCH(PB_KC_NORM, pb::launch_rmsnorm_quant(b, n.w, n.ord, n.domain, stream));
+  }
+
+  // With `norm` given, the matvec's input is that stage of Batch::hidden: fused
+  // into the small-batch matvec's prologue, else a separate launch first.
   void matvec(int wtype, const pb::Batch& b, int columns, const uint8_t* tc_image,
-              std::initializer_list<Mat> mats, int cls, int rt = 32) {
+              std::initializer_list<Mat> mats, int cls, int rt = 32, const Norm* norm = nullptr) {
     using namespace pb;
     if (!b.aq_tc) {
       SmallGemv g{};
@@ -287,11 +300,17 @@ struct pb_engine {
         g.seg[g.nseg].ep = m.ep;
         ++g.nseg;
       }
+      if (norm) {
+        g.norm_weight = norm->w;
+        g.norm_ordinal = norm->ord;
+        g.norm_domain = norm->domain;
+      }
       if (small_gemv_supported(g, b.rows)) {
         PB_LAUNCH(cls, launch_small_gemv(g, b, d_tc_status, stream));
         return;
       }
     }
+    if (norm) norm_launch(b, *norm);
     if (b.aq_tc) {
       TcGemm g{};
       g.wtype = wtype; g.tiles = tc_image; g.nb = columns / 32;
@@ -307,6 +326,20 @@ struct pb_engine {
     } else {
       for (const Mat& m : mats) PB_LAUNCH(cls, launch_qgemv(wtype, m.w, m.rows, columns, b, m.ep, stream));
     }
+  }
+
+  // The sampler over the first n logits rows (history of row i: the slot's
+  // first hist_len[i] tokens); few rows split every row over several CTAs.
+  // Returns the launches made.
+  int sample_rows(uint32_t n, const uint32_t* hist_len) {
+    if (n <= (uint32_t)pb::kSplitSamplerMaxRows) {
+      pb::launch_sampler_split(logits, 151936, (int)n, 151936, history, d_hist_offset, hist_len,
+                               nullptr, d_states, d_sampled, d_cand, stream);
+      return 2;
+    }
+    pb::launch_sampler(logits, 151936, (int)n, 151936, history, d_hist_offset, hist_len, nullptr,
+                       d_states, d_sampled, stream);
+    return 1;
   }
 
   // Runs `enqueue` (the launches of one step) directly or as a CUDA graph
@@ -371,7 +404,8 @@ struct pb_engine {
   // Small batches: gate and up rows of one 32-row block per CTA, SwiGLU and the
   // Q8_0 quantization of the products fused into the matvec.
   bool gateup_swiglu(const pb::Batch& b, const uint8_t* gate_w, const uint8_t* up_w,
-                     const pb::Epilogue& eg, const pb::Epilogue& eu, uint32_t ord) {
+                     const pb::Epilogue& eg, const pb::Epilogue& eu, uint32_t ord,
+                     const Norm& norm) {
     using namespace pb;
     SmallGemv g{};
     g.wtype = W_Q4_0; g.cols = kHidden; g.rt = 32; g.nseg = 2;
@@ -379,6 +413,9 @@ struct pb_engine {
     g.seg[1] = {up_w, kFfn, eu};
     g.swiglu = 1;
     g.swiglu_ordinal = ord;
+    g.norm_weight = norm.w;
+    g.norm_ordinal = norm.ord;
+    g.norm_domain = norm.domain;
     if (!small_gemv_supported(g, b.rows)) return false;
     PB_LAUNCH(PB_KC_GEMV, launch_small_gemv(g, b, d_tc_status, stream));
     return true;
@@ -398,13 +435,12 @@ struct pb_engine {
     for (int layer = 0; layer < kLayers; ++layer) {
       const uint32_t ord = layer + 1;
       auto T = [&](uint32_t role) { return m->tensor(layer_tensor(layer, role)); };
-      PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(T(10)), ord,
-                                                 D_ATTN_NORM, stream));
+      const Norm attn_norm{reinterpret_cast<const float*>(T(10)), ord, D_ATTN_NORM};
       const Epilogue eq{EPI_BIAS, q, kHidden, reinterpret_cast<const float*>(T(18)), err, ord, D_Q};
       const Epilogue ek{EPI_BIAS, k, 128, reinterpret_cast<const float*>(T(15)), err, ord, D_K};
       const Epilogue ev{EPI_BIAS, v, 128, reinterpret_cast<const float*>(T(20)), err, ord, D_V};
       matvec(W_Q4_0, b, 896, m->tc + m->tc_qkv[layer],
-             {{T(19), 896, eq}, {T(16), 128, ek}, {T(21), 128, ev}}, PB_KC_GEMV);
+             {{T(19), 896, eq}, {T(16), 128, ek}, {T(21), 128, ev}}, PB_KC_GEMV, 32, &attn_norm);
       if (distinct_slots) {
         PB_LAUNCH_N(PB_KC_ATTENTION, launch_attention(b, layer, max_span, true, m->rope, stream));
       } else {
@@ -413,15 +449,14 @@ struct pb_engine {
       }
       const Epilogue eo{EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_ATTN_OUTPUT};
       matvec(W_Q4_0, b, 896, m->tc + m->tc_o[layer], {{T(17), 896, eo}}, PB_KC_GEMV, 8);
-      PB_LAUNCH(PB_KC_NORM, launch_rmsnorm_quant(b, reinterpret_cast<const float*>(T(14)), ord,
-                                                 D_FFN_NORM, stream));
+      const Norm ffn_norm{reinterpret_cast<const float*>(T(14)), ord, D_FFN_NORM};
       const Epilogue eg{EPI_STORE, gate, kFfn, nullptr, err, ord, D_GATE};
       const Epilogue eu{EPI_STORE, up, kFfn, nullptr, err, ord, D_UP};
-      if (!b.aq_tc && gateup_swiglu(b, T(12), T(13), eg, eu, ord)) {
-        // gate/up, SwiGLU and its quantization in one small-batch launch
+      if (!b.aq_tc && gateup_swiglu(b, T(12), T(13), eg, eu, ord, ffn_norm)) {
+        // RMSNorm, gate/up, SwiGLU and its quantization in one small-batch launch
       } else {
         matvec(W_Q4_0, b, 896, m->tc + m->tc_gateup[layer], {{T(12), 4864, eg}, {T(13), 4864, eu}},
-               PB_KC_GEMV);
+               PB_KC_GEMV, 32, &ffn_norm);
         PB_LAUNCH(PB_KC_SWIGLU, launch_swiglu_quant(b, ord, stream));
       }
       const Epilogue ed{EPI_RESIDUAL, hidden, kHidden, nullptr, err, ord, D_DOWN};
@@ -757,6 +792,7 @@ uint32_t pb_engine_create(pb_model* model, uint32_t max_seqs, uint32_t max_conte
   chk(dalloc(&e->d_token_log, S * pb_engine::kErrSteps));
   chk(dalloc(&e->d_tc_status, 1));
   chk(dalloc(&e->d_base, S));
+  chk(dalloc(&e->d_cand, pb::split_sampler_words(std::min<int>((int)S, pb::kSplitSamplerMaxRows))));
   chk(dalloc(&e->d_err_cur, R));
   chk(cudaMallocHost(&e->h_tc_status, 4));
   chk(cudaMallocHost(&e->h_slots, R * 4));
@@ -791,7 +827,7 @@ void pb_engine_destroy(pb_engine* e) {
                  e->logits, e->scores, e->aq, e->ad, e->asum, e->d_slots, e->d_positions,
                  e->d_tokens, e->d_err, e->d_greedy, e->d_greedy_bits, e->d_states,
                  e->d_hist_offset, e->d_hist_len, e->d_sampled, e->d_samp_status,
-                 e->d_token_log, e->d_tc_status, e->aq_tc, e->d_base, e->d_err_cur};
+                 e->d_token_log, e->d_tc_status, e->aq_tc, e->d_base, e->d_err_cur, e->d_cand};
   for (void* p : dev) if (p) cudaFree(p);
   void* host[] = {e->h_slots, e->h_positions, e->h_tokens, e->h_err, e->h_greedy, e->h_greedy_bits,
                   e->h_tc_status};
@@ -1078,10 +1114,8 @@ uint32_t pb_engine_sample(pb_engine* e, uint32_t n, const uint32_t* seqs,
   PB_CUDA(cudaMemcpyAsync(e->d_hist_len, len.data(), n * 4, cudaMemcpyHostToDevice, e->stream));
   PB_CUDA(cudaMemcpyAsync(e->d_states, states, n * 16, cudaMemcpyHostToDevice, e->stream));
   e->prof_mark(PB_KC_SAMPLER);
-  pb::launch_sampler(e->logits, 151936, (int)n, 151936, e->history, e->d_hist_offset,
-                     e->d_hist_len, nullptr, e->d_states, e->d_sampled, e->stream);
+  e->launches += e->sample_rows(n, e->d_hist_len);
   e->prof_mark(PB_KC_SAMPLER);
-  e->launches += 1;
   PB_CUDA(cudaGetLastError());
   std::vector<pb::SamplerRow> rows(n);
   PB_CUDA(cudaMemcpyAsync(rows.data(), e->d_sampled, n * sizeof(pb::SamplerRow),
@@ -1148,9 +1182,7 @@ uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
       auto one_step = [&] {
         // history length == position (every evaluated token is in the history)
         e->prof_mark(PB_KC_SAMPLER);
-        pb::launch_sampler(e->logits, 151936, (int)n, 151936, e->history, e->d_hist_offset,
-                           reinterpret_cast<const uint32_t*>(e->d_positions), nullptr, e->d_states,
-                           e->d_sampled, e->stream);
+        e->launches += e->sample_rows(n, reinterpret_cast<const uint32_t*>(e->d_positions)) - 1;
         e->prof_mark(PB_KC_SAMPLER);
         pb::launch_pdl(take_sample_kernel, blocks, threads, 0, e->stream, e->d_sampled,
                        e->d_tokens, e->d_positions, e->d_base, e->d_samp_status, e->d_token_log,

@@ -11,8 +11,11 @@
 // PBTQW25 rows per matrix, fetched into shared memory by cp.async.bulk BEFORE
 // the programmatic-dependency wait, so the weight stream of this launch
 // overlaps the previous kernel.  After the wait:
-//   prologue  the B rows' Q8_0 activations (row-major buffers) into shared
-//             memory;
+//   prologue  the B rows' Q8_0 activations into shared memory: read from the
+//             row-major buffers, or computed from the residual stream as
+//             RMSNorm (fp32_sse2.rs:1310-1334) + quantizer (fp32_sse2.rs:
+//             945-983), every CTA repeating that small exact computation
+//             instead of a separate launch;
 //   phase 1   every (row, block) item: the B block dots and terms into shared
 //             memory;
 //   phase 2   every (sequence, row): the binary32 sum in block order, then the
@@ -44,6 +47,73 @@ __device__ __forceinline__ uint32_t ld_u32_2aligned_s(const uint8_t* p) {
   const uint32_t lo = *reinterpret_cast<const uint16_t*>(p);
   const uint32_t hi = *reinterpret_cast<const uint16_t*>(p + 2);
   return lo | (hi << 16);
+}
+
+// Q8_0 quantization of one 32-element block by one thread (fp32_sse2.rs:945-983):
+// the same operations as quantize_lane, serially; y holds the block's values.
+__device__ __forceinline__ void quantize_block_serial(const float* y, int8_t* aq, float* ad,
+                                                      int* asum) {
+  float amax = fabsf(y[0]);
+#pragma unroll 8
+  for (int j = 1; j < 32; ++j) amax = fmaxf(amax, fabsf(y[j]));
+  const float d = __fdiv_rn(amax, 127.0f);
+  const float inverse = bitsf(d) == 0 ? 0.0f : __fdiv_rn(1.0f, d);
+  int total = 0;
+  uint32_t word = 0;
+#pragma unroll 8
+  for (int j = 0; j < 32; ++j) {
+    const float v = __fmul_rn(y[j], inverse);
+    const float half = (bitsf(v) >> 31) == 0 ? 0.5f : -0.5f;
+    const float t = __fadd_rn(v, half);
+    const int q = fabsf(t) < 2147483648.0f ? __float2int_rz(t) : (int)0x80000000u;
+    total += (int)(int8_t)q;
+    word |= (uint32_t)(uint8_t)q << (8 * (j & 3));
+    if ((j & 3) == 3) {
+      reinterpret_cast<uint32_t*>(aq)[j >> 2] = word;
+      word = 0;
+    }
+  }
+  *ad = __half2float(__float2half_rn(d));
+  *asum = total;
+}
+
+// RMSNorm (fp32_sse2.rs:1310-1334) of row s of x by one warp into y (block-major,
+// 33 words per 32-element block): the 896 f64 squares summed as a tree when the
+// exponent span proves it equal to the serial sum (rmsnorm_quant_kernel), else
+// serially by lane 0.
+__device__ void norm_row_warp(const float* __restrict__ x, const float* __restrict__ w, float* y,
+                              unsigned long long* err, uint32_t ordinal, uint32_t domain) {
+  const int lane = threadIdx.x & 31;
+  double sum = 0.0;
+  int emin = 255, emax = 0;
+  for (int e = lane; e < kHidden; e += 32) {
+    const float q = __fmul_rn(x[e], x[e]);
+    sum += (double)q;
+    const uint32_t qb = bitsf(q) & 0x7fffffffu;
+    const int ex = (int)(qb >> 23);
+    if (qb != 0) {
+      emin = min(emin, max(ex, 1));
+      emax = max(emax, max(ex, 1));
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    emin = min(emin, __shfl_xor_sync(0xffffffffu, emin, o));
+    emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
+  }
+  if (emax == 255 || (emax >= emin && emax - emin > 19)) {
+    double serial = 0.0;
+    if (lane == 0)
+      for (int e = 0; e < kHidden; ++e) serial += (double)__fmul_rn(x[e], x[e]);
+    sum = __shfl_sync(0xffffffffu, serial, 0);
+  }
+  const float mean = (float)(sum / 896.0);
+  const float inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, fbits(0x358637bdu))));
+  for (int e = lane; e < kHidden; e += 32) {
+    const float v = __fmul_rn(__fmul_rn(x[e], inverse), w[e]);
+    check_finite(v, err, ordinal, domain, 0, e);
+    y[(e >> 5) * 33 + (e & 31)] = v;
+  }
 }
 
 template <int BPB>
@@ -96,7 +166,20 @@ small_gemv_kernel(SmallGemv g, Batch b, unsigned int* status) {
   pdl_wait();
 
   // ---- the B rows' Q8_0 activations into shared memory
-  {
+  if (g.norm_weight) {
+    // RMSNorm of each row (a warp per row) into the term buffer, then one
+    // thread per (row, block) quantizes
+    float* ys = terms;
+    for (int s = warp; s < B; s += kSgThreads / 32)
+      norm_row_warp(b.hidden + (size_t)s * kHidden, g.norm_weight, ys + s * (kHidden / 32) * 33,
+                    &b.err[s], g.norm_ordinal, g.norm_domain);
+    __syncthreads();
+    for (int i = tid; i < B * nb; i += kSgThreads) {
+      const int s = i / nb, k = i % nb;
+      quantize_block_serial(ys + (s * nb + k) * 33, aq_s + (size_t)s * g.cols + k * 32,
+                            ad_s + i, asum_s + i);
+    }
+  } else {
     const int chunks = g.cols / 16;
     for (int i = tid; i < B * chunks; i += kSgThreads) {
       const int s = i / chunks, c = i % chunks;
@@ -232,7 +315,8 @@ size_t small_gemv_smem(const SmallGemv& g, int B) {
   const int rows_cta = g.rt * (g.swiglu ? 2 : 1);
   const size_t wbytes = ((size_t)rows_cta * nb * bpb + 15) & ~(size_t)15;
   const size_t act = (size_t)B * g.cols + (size_t)B * nb * 8;
-  const size_t tbytes = (size_t)B * rows_cta * (nb + 1) * 4;
+  size_t tbytes = (size_t)B * rows_cta * (nb + 1) * 4;
+  if (g.norm_weight) tbytes = std::max(tbytes, (size_t)B * (kHidden / 32) * 33 * 4);
   return 16 + wbytes + act + tbytes;
 }
 
@@ -240,6 +324,7 @@ size_t small_gemv_smem(const SmallGemv& g, int B) {
 
 bool small_gemv_supported(const SmallGemv& g, int B) {
   if (B < 1 || B > 8 || g.rt <= 0 || g.cols % 32) return false;
+  if (g.norm_weight && g.cols != kHidden) return false;
   const int bpb = g.wtype == W_Q4_0 ? 18 : 34;
   if (((size_t)g.rt * (g.cols / 32) * bpb) % 16) return false;  // bulk copy size
   if (g.swiglu && (g.rt != 32 || g.nseg != 2 || g.seg[0].rows_end != g.seg[1].rows_end))

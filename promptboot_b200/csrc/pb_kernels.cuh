@@ -165,6 +165,11 @@ struct SmallGemv {
   } seg[3];
   int swiglu;
   uint32_t swiglu_ordinal;
+  // Optional RMSNorm + Q8_0 prologue (cols 896): the activations are computed
+  // from Batch::hidden with this norm weight instead of read from Batch::aq,
+  // every CTA repeating the small exact computation instead of a separate launch.
+  const float* norm_weight = nullptr;
+  uint32_t norm_ordinal = 0, norm_domain = 0;
 };
 bool small_gemv_supported(const SmallGemv& g, int batch);
 // Sets *status (device word) if a weight copy did not land in time.
@@ -204,6 +209,16 @@ void launch_sampler(float* logits, size_t ld, int rows, int words, const uint32_
                     const uint64_t* hist_offset, const uint32_t* hist_len,
                     const uint8_t* initial_seen, unsigned long long* states, SamplerRow* out,
                     cudaStream_t s);
+// The same sampler for few rows: each row's vocabulary split over kSplitParts
+// CTAs, then one merge CTA per row (two launches).  cand: device scratch of
+// split_sampler_words(rows) 64-bit words.
+constexpr int kSplitParts = 32;
+constexpr int kSplitSamplerMaxRows = 32;
+constexpr size_t split_sampler_words(int rows) { return (size_t)rows * kSplitParts * 21; }
+void launch_sampler_split(float* logits, size_t ld, int rows, int words, const uint32_t* history,
+                          const uint64_t* hist_offset, const uint32_t* hist_len,
+                          const uint8_t* initial_seen, unsigned long long* states, SamplerRow* out,
+                          unsigned long long* cand, cudaStream_t s);
 
 void init_kernel_attributes();
 

@@ -49,10 +49,11 @@ struct RowScratch {
   unsigned long long* state = nullptr;
   pb::SamplerRow* out = nullptr;
   uint32_t* pairs = nullptr;
+  unsigned long long* cand = nullptr;  // the split sampler's part lists
   ~RowScratch() {
     if (device < 0) return;
     cudaSetDevice(device);
-    void* p[] = {logits, history, offset, length, seen, state, out, pairs};
+    void* p[] = {logits, history, offset, length, seen, state, out, pairs, cand};
     for (void* x : p) if (x) cudaFree(x);
     if (stream) cudaStreamDestroy(stream);
   }
@@ -66,6 +67,7 @@ struct RowScratch {
     PB_CUDA(cudaMalloc(&out, sizeof(pb::SamplerRow)));
     PB_CUDA(cudaMalloc(&seen, PB_SEEN_BYTES));
     PB_CUDA(cudaMalloc(&pairs, 16 * 4));
+    PB_CUDA(cudaMalloc(&cand, pb::split_sampler_words(1) * 8));
     const uint64_t zero = 0;
     PB_CUDA(cudaMemcpyAsync(offset, &zero, 8, cudaMemcpyHostToDevice, stream));
     PB_CUDA(cudaStreamSynchronize(stream));
@@ -116,8 +118,8 @@ uint32_t run_sampler_row(uint32_t* logits, const uint32_t* tokens, uint64_t coun
   PB_CUDA(cudaMemcpyAsync(s->length, &n, 4, cudaMemcpyHostToDevice, stream));
   PB_CUDA(cudaMemcpyAsync(s->state, state, 16, cudaMemcpyHostToDevice, stream));
   if (seen) PB_CUDA(cudaMemcpyAsync(s->seen, seen, PB_SEEN_BYTES, cudaMemcpyHostToDevice, stream));
-  pb::launch_sampler(s->logits, kV, 1, (int)kV, s->history, s->offset, s->length,
-                     seen ? s->seen : nullptr, s->state, s->out, stream);
+  pb::launch_sampler_split(s->logits, kV, 1, (int)kV, s->history, s->offset, s->length,
+                           seen ? s->seen : nullptr, s->state, s->out, s->cand, stream);
   PB_CUDA(cudaGetLastError());
   PB_CUDA(cudaMemcpyAsync(row, s->out, sizeof(pb::SamplerRow), cudaMemcpyDeviceToHost, stream));
   PB_CUDA(cudaStreamSynchronize(stream));

@@ -71,14 +71,15 @@ __device__ __forceinline__ unsigned long long make_key(float v, uint32_t id) {
   return ((unsigned long long)order_key(v) << 32) | (unsigned long long)(~id);
 }
 
-// Streams [0, words) of one row, folding every element into the CTA's top-K.
-// penal (may be null) marks ids whose value is penalised before ranking.
+// Streams [0, words) of one row (or of a slice of it whose first id is
+// id_base), folding every element into the CTA's top-K.  penal (may be null)
+// marks the slice's ids whose value is penalised before ranking.
 // Leaves the final list sorted in `out_keys[0..K)` (shared) and the first
 // non-finite index/bits in *bad (shared, ~0 when none).
 template <int K>
 __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t* penal,
                          unsigned long long* warp_keys, unsigned long long* out_keys,
-                         unsigned long long* bad) {
+                         unsigned long long* bad, int id_base = 0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int seg = ((words + kSampWarps * 128 - 1) / (kSampWarps * 128)) * 128;
   const int start = warp * seg;
@@ -96,7 +97,7 @@ __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t*
     unsigned long long key = 0;
     if (i < end && val >= thr_f) {
       if (penal && (penal[i >> 5] >> (i & 31) & 1u)) val = penalize(val);
-      key = make_key(val, (uint32_t)i);
+      key = make_key(val, (uint32_t)(id_base + i));
     }
     list_offer<K>(entry, thr, key, lane);
     thr_f = thr == 0 ? fbits(0xff800000u) : key_value(thr);
@@ -156,7 +157,7 @@ __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t*
     // some value is not finite: the first one, in index order
     for (int i = threadIdx.x; i < words; i += blockDim.x) {
       const uint32_t vb = bitsf(x[i]);
-      if (!finite_bits(vb)) atomicMin(bad, ((unsigned long long)i << 32) | vb);
+      if (!finite_bits(vb)) atomicMin(bad, ((unsigned long long)(id_base + i) << 32) | vb);
     }
     __syncthreads();
   }
@@ -172,59 +173,12 @@ __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t*
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kSampThreads)
-sampler_kernel(float* logits, size_t ld, int words, const uint32_t* __restrict__ history,
-               const uint64_t* __restrict__ hist_offset, const uint32_t* __restrict__ hist_len,
-               const uint8_t* __restrict__ initial_seen, unsigned long long* states,
-               SamplerRow* out) {
-  pdl_begin();
-  __shared__ uint32_t penal[(kVocab + 31) / 32];
-  __shared__ unsigned long long warp_keys[kSampWarps * 20];
-  __shared__ unsigned long long top[20];
-  __shared__ unsigned long long bad;
-  __shared__ unsigned long long bad_token;
-  const int row = blockIdx.x;
-  float* x = logits + (size_t)row * ld;
-  const uint32_t* hist = history + hist_offset[row];
-  const uint32_t n = hist_len[row];
-  const int map_words = (words + 31) / 32;
-
-  for (int i = threadIdx.x; i < map_words; i += blockDim.x) penal[i] = 0;
-  if (threadIdx.x == 0) { bad = kNoError; bad_token = kNoError; }
-  __syncthreads();
-  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
-    uint32_t t = hist[j];
-    if (t < (uint32_t)words) atomicOr(&penal[t >> 5], 1u << (t & 31));
-    else atomicMin(&bad_token, ((unsigned long long)j << 32) | t);
-  }
-  __syncthreads();
-  if (initial_seen) {
-    // Tokens already marked in the caller's bitmap are skipped by the reference.
-    for (int i = threadIdx.x; i < map_words; i += blockDim.x) {
-      uint32_t m = 0;
-      for (int byte = 0; byte < 4; ++byte) {
-        int at = i * 4 + byte;
-        if (at < (words + 7) / 8) m |= (uint32_t)initial_seen[at] << (8 * byte);
-      }
-      penal[i] &= ~m;
-    }
-    __syncthreads();
-  }
-
-  row_topk<20>(x, words, penal, warp_keys, top, &bad);
-
-  const bool ok = bad == kNoError && bad_token == kNoError;
-  if (ok) {
-    // Write the penalised logits back in place, once per distinct token.
-    for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
-      uint32_t t = hist[j];
-      uint32_t bit = 1u << (t & 31);
-      uint32_t old = atomicAnd(&penal[t >> 5], ~bit);
-      if (old & bit) x[t] = penalize(x[t]);
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x != 0) return;
+// The draw and top-k/top-p of one row (fp32_sse2.rs:1818-1845, inference.rs:
+// 801-809) from its final sorted top-20 keys, or its rejection: the first
+// non-finite logit (status 7) before the first history id out of range (3).
+__device__ void sample_tail(const unsigned long long* top, unsigned long long bad,
+                            unsigned long long bad_token, unsigned long long* states,
+                            SamplerRow* out, int row) {
   SamplerRow r;
   r.selected = 0;
   if (bad != kNoError) {
@@ -285,12 +239,198 @@ sampler_kernel(float* logits, size_t ld, int words, const uint32_t* __restrict__
   out[row] = r;
 }
 
+__global__ void __launch_bounds__(kSampThreads)
+sampler_kernel(float* logits, size_t ld, int words, const uint32_t* __restrict__ history,
+               const uint64_t* __restrict__ hist_offset, const uint32_t* __restrict__ hist_len,
+               const uint8_t* __restrict__ initial_seen, unsigned long long* states,
+               SamplerRow* out) {
+  pdl_begin();
+  __shared__ uint32_t penal[(kVocab + 31) / 32];
+  __shared__ unsigned long long warp_keys[kSampWarps * 20];
+  __shared__ unsigned long long top[20];
+  __shared__ unsigned long long bad;
+  __shared__ unsigned long long bad_token;
+  const int row = blockIdx.x;
+  float* x = logits + (size_t)row * ld;
+  const uint32_t* hist = history + hist_offset[row];
+  const uint32_t n = hist_len[row];
+  const int map_words = (words + 31) / 32;
+
+  for (int i = threadIdx.x; i < map_words; i += blockDim.x) penal[i] = 0;
+  if (threadIdx.x == 0) { bad = kNoError; bad_token = kNoError; }
+  __syncthreads();
+  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+    uint32_t t = hist[j];
+    if (t < (uint32_t)words) atomicOr(&penal[t >> 5], 1u << (t & 31));
+    else atomicMin(&bad_token, ((unsigned long long)j << 32) | t);
+  }
+  __syncthreads();
+  if (initial_seen) {
+    // Tokens already marked in the caller's bitmap are skipped by the reference.
+    for (int i = threadIdx.x; i < map_words; i += blockDim.x) {
+      uint32_t m = 0;
+      for (int byte = 0; byte < 4; ++byte) {
+        int at = i * 4 + byte;
+        if (at < (words + 7) / 8) m |= (uint32_t)initial_seen[at] << (8 * byte);
+      }
+      penal[i] &= ~m;
+    }
+    __syncthreads();
+  }
+
+  row_topk<20>(x, words, penal, warp_keys, top, &bad);
+
+  const bool ok = bad == kNoError && bad_token == kNoError;
+  if (ok) {
+    // Write the penalised logits back in place, once per distinct token.
+    for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+      uint32_t t = hist[j];
+      uint32_t bit = 1u << (t & 31);
+      uint32_t old = atomicAnd(&penal[t >> 5], ~bit);
+      if (old & bit) x[t] = penalize(x[t]);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) sample_tail(top, bad, bad_token, states, out, row);
+}
+
 void launch_sampler(float* logits, size_t ld, int rows, int words, const uint32_t* history,
                     const uint64_t* hist_offset, const uint32_t* hist_len,
                     const uint8_t* initial_seen, unsigned long long* states, SamplerRow* out,
                     cudaStream_t s) {
   launch_pdl(sampler_kernel, rows, kSampThreads, 0, s, logits, ld, words, history, hist_offset,
                                                hist_len, initial_seen, states, out);
+}
+
+// ------------------------------------------------------ split rows
+//
+// Few rows leave most SMs idle with one CTA per row, so a row's vocabulary
+// is split over kSplitParts CTAs: each ranks its slice (penalised by the
+// history tokens that fall in it) into a top-20 of global ids; a merge CTA per
+// row then folds the parts' lists (the same keys, so the same order and ties
+// as one scan), writes the penalised logits back once per distinct history
+// token and draws, exactly as sampler_kernel does.
+constexpr int kSplitSlice = ((kVocab + kSplitParts - 1) / kSplitParts + 127) / 128 * 128;
+
+__global__ void __launch_bounds__(kSampThreads)
+sampler_part_kernel(const float* logits, size_t ld, int words, const uint32_t* __restrict__ history,
+                    const uint64_t* __restrict__ hist_offset, const uint32_t* __restrict__ hist_len,
+                    const uint8_t* __restrict__ initial_seen, unsigned long long* cand) {
+  pdl_begin();
+  __shared__ uint32_t penal[kSplitSlice / 32];
+  __shared__ unsigned long long warp_keys[kSampWarps * 20];
+  __shared__ unsigned long long top[20];
+  __shared__ unsigned long long bad;
+  const int row = blockIdx.x, part = blockIdx.y;
+  const int lo = part * kSplitSlice, hi = min(words, lo + kSplitSlice);
+  unsigned long long* mine = cand + ((size_t)row * kSplitParts + part) * 21;
+  if (lo >= hi) {  // an empty tail part
+    if (threadIdx.x < 20) mine[threadIdx.x] = 0;
+    if (threadIdx.x == 0) mine[20] = kNoError;
+    return;
+  }
+  const float* x = logits + (size_t)row * ld;
+  const uint32_t* hist = history + hist_offset[row];
+  const uint32_t n = hist_len[row];
+  const int map_words = (hi - lo + 31) / 32;
+  for (int i = threadIdx.x; i < map_words; i += blockDim.x) penal[i] = 0;
+  if (threadIdx.x == 0) bad = kNoError;
+  __syncthreads();
+  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+    const uint32_t t = hist[j];
+    if (t >= (uint32_t)lo && t < (uint32_t)hi) atomicOr(&penal[(t - lo) >> 5], 1u << ((t - lo) & 31));
+  }
+  __syncthreads();
+  if (initial_seen) {
+    // tokens already marked in the caller's bitmap are skipped (lo is a
+    // multiple of 32, so slice word i is seen bytes 4 (lo / 32 + i) ..)
+    for (int i = threadIdx.x; i < map_words; i += blockDim.x) {
+      uint32_t m = 0;
+      for (int byte = 0; byte < 4; ++byte) {
+        const int at = (lo >> 3) + i * 4 + byte;
+        if (at < (words + 7) / 8) m |= (uint32_t)initial_seen[at] << (8 * byte);
+      }
+      penal[i] &= ~m;
+    }
+    __syncthreads();
+  }
+  row_topk<20>(x + lo, hi - lo, penal, warp_keys, top, &bad, lo);
+  if (threadIdx.x < 20) mine[threadIdx.x] = top[threadIdx.x];
+  if (threadIdx.x == 0) mine[20] = bad;
+}
+
+__global__ void __launch_bounds__(kSampThreads)
+sampler_merge_kernel(float* logits, size_t ld, int words, const uint32_t* __restrict__ history,
+                     const uint64_t* __restrict__ hist_offset, const uint32_t* __restrict__ hist_len,
+                     const uint8_t* __restrict__ initial_seen, const unsigned long long* cand,
+                     unsigned long long* states, SamplerRow* out) {
+  pdl_begin();
+  __shared__ uint32_t penal[(kVocab + 31) / 32];
+  __shared__ unsigned long long top[20];
+  __shared__ unsigned long long bad;
+  __shared__ unsigned long long bad_token;
+  const int row = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* x = logits + (size_t)row * ld;
+  const uint32_t* hist = history + hist_offset[row];
+  const uint32_t n = hist_len[row];
+  const int map_words = (words + 31) / 32;
+  const unsigned long long* rc = cand + (size_t)row * kSplitParts * 21;
+  for (int i = threadIdx.x; i < map_words; i += blockDim.x) penal[i] = 0;
+  if (threadIdx.x == 0) {
+    unsigned long long b0 = kNoError;
+    for (int part = 0; part < kSplitParts; ++part) b0 = min(b0, rc[part * 21 + 20]);
+    bad = b0;
+    bad_token = kNoError;
+  }
+  __syncthreads();
+  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+    const uint32_t t = hist[j];
+    if (t < (uint32_t)words) atomicOr(&penal[t >> 5], 1u << (t & 31));
+    else atomicMin(&bad_token, ((unsigned long long)j << 32) | t);
+  }
+  if (warp == 0) {
+    unsigned long long entry = 0, thr = 0;
+    for (int base = 0; base < kSplitParts * 20; base += 32) {
+      const int at = base + lane;
+      const unsigned long long key = at < kSplitParts * 20 ? rc[(at / 20) * 21 + at % 20] : 0ull;
+      list_offer<20>(entry, thr, key, lane);
+    }
+    if (lane < 20) top[lane] = entry;
+  }
+  __syncthreads();
+  if (initial_seen) {
+    for (int i = threadIdx.x; i < map_words; i += blockDim.x) {
+      uint32_t m = 0;
+      for (int byte = 0; byte < 4; ++byte) {
+        const int at = i * 4 + byte;
+        if (at < (words + 7) / 8) m |= (uint32_t)initial_seen[at] << (8 * byte);
+      }
+      penal[i] &= ~m;
+    }
+    __syncthreads();
+  }
+  if (bad == kNoError && bad_token == kNoError) {
+    // the penalised logits back in place, once per distinct token
+    for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+      const uint32_t t = hist[j];
+      const uint32_t bit = 1u << (t & 31);
+      const uint32_t old = atomicAnd(&penal[t >> 5], ~bit);
+      if (old & bit) x[t] = penalize(x[t]);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) sample_tail(top, bad, bad_token, states, out, row);
+}
+
+void launch_sampler_split(float* logits, size_t ld, int rows, int words, const uint32_t* history,
+                          const uint64_t* hist_offset, const uint32_t* hist_len,
+                          const uint8_t* initial_seen, unsigned long long* states, SamplerRow* out,
+                          unsigned long long* cand, cudaStream_t s) {
+  launch_pdl(sampler_part_kernel, dim3(rows, kSplitParts), kSampThreads, 0, s, logits, ld, words,
+             history, hist_offset, hist_len, initial_seen, cand);
+  launch_pdl(sampler_merge_kernel, rows, kSampThreads, 0, s, logits, ld, words, history, hist_offset,
+             hist_len, initial_seen, cand, states, out);
 }
 
 // inference.rs:814-859 top_logits_8: descending, equal values (and signed zeros)

@@ -272,3 +272,52 @@ def test_device_batch_sampler_ties_match_oracle(case):
                                                   512, oracle._p(seen))
         assert got[r, 0] == 0 and got[r, 3] == oracle.sample_top_k_top_p(ref_logits, draws[r]), r
         assert np.array_equal(f32bits(mutated[r]), f32bits(ref_logits)), r
+
+
+@pytest.mark.parametrize("case", ["all_equal", "signed_zero_top", "duplicate_top", "penalty_ties",
+                                  "slice_edges", "nonfinite_late"])
+def test_split_row_sampler_matches_oracle(case):
+    """The host-buffer sampler, which splits the row's vocabulary over several
+    CTAs and merges their top-20 lists: the tie cases above, the best values
+    on the slice boundaries (ids 4863/4864, the last id), and a non-finite word
+    in the last slice (the reference's first-non-finite error)."""
+    rng = np.random.default_rng(sum(map(ord, case)) + 5)
+    logits = (rng.standard_normal(V) * 3.0).astype(np.float32)
+    history = rng.integers(0, V, size=300, dtype=np.uint32)
+    if case == "all_equal":
+        logits[:] = np.float32(1.25)
+    elif case == "signed_zero_top":
+        logits = -np.abs(logits) - np.float32(1.0)
+        idx = rng.choice(V, 30, replace=False)
+        logits[idx[:15]] = np.float32(0.0)
+        logits[idx[15:]] = np.float32(-0.0)
+    elif case == "duplicate_top":
+        logits[rng.choice(V, 40, replace=False)] = np.float32(14.0)
+    elif case == "penalty_ties":
+        logits[int(history[0])] = np.float32(11.0)
+        logits[rng.choice(V, 25, replace=False)] = np.float32(np.float32(11.0) / np.float32(1.1))
+    elif case == "slice_edges":
+        for i, t in enumerate([4863, 4864, 9727, 9728, V - 1, 0, 150783, 150784]):
+            logits[t] = np.float32(13.0 - 0.25 * (i % 3))
+        history[:3] = [4864, V - 1, 0]
+    else:
+        logits[V - 7] = np.float32(np.inf)
+    bits = f32bits(logits).copy()
+    seen = np.zeros(api.SEEN_BYTES, dtype=np.uint8)
+    state = api.SamplingState(31)
+    ref = logits.copy()
+    ref_state = oracle.SamplingState(31)
+    st_ref, id_ref, err_ref = oracle.sample_with_repetition(ref, history, ref_state)
+    if case == "nonfinite_late":
+        assert st_ref != 0
+        with pytest.raises(api.InferenceError) as exc:
+            api.sample_token_with_repetition(bits, history, seen, state)
+        e = exc.value
+        assert (e.status, e.domain, e.available, e.detail) == \
+            (err_ref.status, err_ref.domain, err_ref.available, err_ref.detail)
+        return
+    assert st_ref == 0
+    got = api.sample_token_with_repetition(bits, history, seen, state)
+    assert got == id_ref
+    assert state.state() == int(ref_state.state[0]) and state.draws() == 1
+    assert np.array_equal(bits, f32bits(ref))
