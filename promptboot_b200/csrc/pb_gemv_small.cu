@@ -77,8 +77,8 @@ __device__ __forceinline__ void quantize_block_serial(const float* y, int8_t* aq
   *asum = total;
 }
 
-// RMSNorm (fp32_sse2.rs:1310-1334) of row s of x by one warp into y (block-major,
-// 33 words per 32-element block): the 896 f64 squares summed as a tree when the
+// RMSNorm (fp32_sse2.rs:1310-1334) of one row x (shared memory) by one warp into
+// y (block-major, 33 words per 32-element block): the 896 f64 squares summed as a tree when the
 // exponent span proves it equal to the serial sum (rmsnorm_quant_kernel), else
 // serially by lane 0.
 __device__ void norm_row_warp(const float* __restrict__ x, const float* __restrict__ w, float* y,
@@ -167,12 +167,23 @@ small_gemv_kernel(SmallGemv g, Batch b, unsigned int* status) {
 
   // ---- the B rows' Q8_0 activations into shared memory
   if (g.norm_weight) {
-    // RMSNorm of each row (a warp per row) into the term buffer, then one
-    // thread per (row, block) quantizes
+    // The B rows and the norm weight staged into shared memory with every
+    // load in flight at once, RMSNorm of each row (a warp per row) into the
+    // term buffer, then one thread per (row, block) quantizes.
     float* ys = terms;
+    float* xs = ys + B * (kHidden / 32) * 33;
+    float* wsm = xs + B * kHidden;
+    for (int i = tid; i < B * (kHidden / 4); i += kSgThreads) {
+      const int s = i / (kHidden / 4), c = i % (kHidden / 4);
+      reinterpret_cast<float4*>(xs + s * kHidden)[c] =
+          reinterpret_cast<const float4*>(b.hidden + (size_t)s * kHidden)[c];
+    }
+    for (int i = tid; i < kHidden / 4; i += kSgThreads)
+      reinterpret_cast<float4*>(wsm)[i] = reinterpret_cast<const float4*>(g.norm_weight)[i];
+    __syncthreads();
     for (int s = warp; s < B; s += kSgThreads / 32)
-      norm_row_warp(b.hidden + (size_t)s * kHidden, g.norm_weight, ys + s * (kHidden / 32) * 33,
-                    &b.err[s], g.norm_ordinal, g.norm_domain);
+      norm_row_warp(xs + s * kHidden, wsm, ys + s * (kHidden / 32) * 33, &b.err[s], g.norm_ordinal,
+                    g.norm_domain);
     __syncthreads();
     for (int i = tid; i < B * nb; i += kSgThreads) {
       const int s = i / nb, k = i % nb;
@@ -316,7 +327,8 @@ size_t small_gemv_smem(const SmallGemv& g, int B) {
   const size_t wbytes = ((size_t)rows_cta * nb * bpb + 15) & ~(size_t)15;
   const size_t act = (size_t)B * g.cols + (size_t)B * nb * 8;
   size_t tbytes = (size_t)B * rows_cta * (nb + 1) * 4;
-  if (g.norm_weight) tbytes = std::max(tbytes, (size_t)B * (kHidden / 32) * 33 * 4);
+  if (g.norm_weight)
+    tbytes = std::max(tbytes, ((size_t)B * ((kHidden / 32) * 33 + kHidden) + kHidden) * 4);
   return 16 + wbytes + act + tbytes;
 }
 

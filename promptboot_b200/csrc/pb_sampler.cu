@@ -71,17 +71,35 @@ __device__ __forceinline__ unsigned long long make_key(float v, uint32_t id) {
   return ((unsigned long long)order_key(v) << 32) | (unsigned long long)(~id);
 }
 
+// The K largest of n keys (nonzero keys distinct: every id is in one list
+// only; 0 marks an empty entry) into out_keys in descending order, by rank:
+// each nonzero key counts the keys above it, the whole CTA at once.  Ends with
+// a CTA barrier.
+template <int K>
+__device__ void merge_ranked(const unsigned long long* keys, int n, unsigned long long* out_keys) {
+  if (threadIdx.x < K) out_keys[threadIdx.x] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long k = keys[i];
+    if (k == 0) continue;
+    int rank = 0;
+    for (int j = 0; j < n; ++j) rank += keys[j] > k ? 1 : 0;
+    if (rank < K) out_keys[rank] = k;
+  }
+  __syncthreads();
+}
+
 // Streams [0, words) of one row (or of a slice of it whose first id is
 // id_base), folding every element into the CTA's top-K.  penal (may be null)
 // marks the slice's ids whose value is penalised before ranking.
 // Leaves the final list sorted in `out_keys[0..K)` (shared) and the first
 // non-finite index/bits in *bad (shared, ~0 when none).
-template <int K>
+template <int K, int NW = kSampWarps>
 __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t* penal,
                          unsigned long long* warp_keys, unsigned long long* out_keys,
                          unsigned long long* bad, int id_base = 0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int seg = ((words + kSampWarps * 128 - 1) / (kSampWarps * 128)) * 128;
+  const int seg = ((words + NW * 128 - 1) / (NW * 128)) * 128;
   const int start = warp * seg;
   const int end = min(words, start + seg);
   unsigned long long entry = 0, thr = 0;
@@ -161,16 +179,7 @@ __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t*
     }
     __syncthreads();
   }
-  if (warp == 0) {
-    entry = 0;
-    thr = 0;
-    for (int base = 0; base < kSampWarps * K; base += 32) {
-      unsigned long long key = (base + lane < kSampWarps * K) ? warp_keys[base + lane] : 0ull;
-      list_offer<K>(entry, thr, key, lane);
-    }
-    if (lane < K) out_keys[lane] = entry;
-  }
-  __syncthreads();
+  merge_ranked<K>(warp_keys, NW * K, out_keys);
 }
 
 // The draw and top-k/top-p of one row (fp32_sse2.rs:1818-1845, inference.rs:
@@ -312,13 +321,15 @@ void launch_sampler(float* logits, size_t ld, int rows, int words, const uint32_
 // token and draws, exactly as sampler_kernel does.
 constexpr int kSplitSlice = ((kVocab + kSplitParts - 1) / kSplitParts + 127) / 128 * 128;
 
-__global__ void __launch_bounds__(kSampThreads)
+constexpr int kPartWarps = 4;
+
+__global__ void __launch_bounds__(kPartWarps * 32)
 sampler_part_kernel(const float* logits, size_t ld, int words, const uint32_t* __restrict__ history,
                     const uint64_t* __restrict__ hist_offset, const uint32_t* __restrict__ hist_len,
                     const uint8_t* __restrict__ initial_seen, unsigned long long* cand) {
   pdl_begin();
   __shared__ uint32_t penal[kSplitSlice / 32];
-  __shared__ unsigned long long warp_keys[kSampWarps * 20];
+  __shared__ unsigned long long warp_keys[kPartWarps * 20];
   __shared__ unsigned long long top[20];
   __shared__ unsigned long long bad;
   const int row = blockIdx.x, part = blockIdx.y;
@@ -354,7 +365,7 @@ sampler_part_kernel(const float* logits, size_t ld, int words, const uint32_t* _
     }
     __syncthreads();
   }
-  row_topk<20>(x + lo, hi - lo, penal, warp_keys, top, &bad, lo);
+  row_topk<20, kPartWarps>(x + lo, hi - lo, penal, warp_keys, top, &bad, lo);
   if (threadIdx.x < 20) mine[threadIdx.x] = top[threadIdx.x];
   if (threadIdx.x == 0) mine[20] = bad;
 }
@@ -366,11 +377,11 @@ sampler_merge_kernel(float* logits, size_t ld, int words, const uint32_t* __rest
                      unsigned long long* states, SamplerRow* out) {
   pdl_begin();
   __shared__ uint32_t penal[(kVocab + 31) / 32];
+  __shared__ unsigned long long part_keys[kSplitParts * 20];
   __shared__ unsigned long long top[20];
   __shared__ unsigned long long bad;
   __shared__ unsigned long long bad_token;
   const int row = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float* x = logits + (size_t)row * ld;
   const uint32_t* hist = history + hist_offset[row];
   const uint32_t n = hist_len[row];
@@ -389,16 +400,10 @@ sampler_merge_kernel(float* logits, size_t ld, int words, const uint32_t* __rest
     if (t < (uint32_t)words) atomicOr(&penal[t >> 5], 1u << (t & 31));
     else atomicMin(&bad_token, ((unsigned long long)j << 32) | t);
   }
-  if (warp == 0) {
-    unsigned long long entry = 0, thr = 0;
-    for (int base = 0; base < kSplitParts * 20; base += 32) {
-      const int at = base + lane;
-      const unsigned long long key = at < kSplitParts * 20 ? rc[(at / 20) * 21 + at % 20] : 0ull;
-      list_offer<20>(entry, thr, key, lane);
-    }
-    if (lane < 20) top[lane] = entry;
-  }
+  for (int i = threadIdx.x; i < kSplitParts * 20; i += blockDim.x)
+    part_keys[i] = rc[(i / 20) * 21 + i % 20];
   __syncthreads();
+  merge_ranked<20>(part_keys, kSplitParts * 20, top);
   if (initial_seen) {
     for (int i = threadIdx.x; i < map_words; i += blockDim.x) {
       uint32_t m = 0;
@@ -427,7 +432,7 @@ void launch_sampler_split(float* logits, size_t ld, int rows, int words, const u
                           const uint64_t* hist_offset, const uint32_t* hist_len,
                           const uint8_t* initial_seen, unsigned long long* states, SamplerRow* out,
                           unsigned long long* cand, cudaStream_t s) {
-  launch_pdl(sampler_part_kernel, dim3(rows, kSplitParts), kSampThreads, 0, s, logits, ld, words,
+  launch_pdl(sampler_part_kernel, dim3(rows, kSplitParts), kPartWarps * 32, 0, s, logits, ld, words,
              history, hist_offset, hist_len, initial_seen, cand);
   launch_pdl(sampler_merge_kernel, rows, kSampThreads, 0, s, logits, ld, words, history, hist_offset,
              hist_len, initial_seen, cand, states, out);
