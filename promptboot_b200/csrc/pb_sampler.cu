@@ -179,7 +179,18 @@ __device__ void row_topk(const float* __restrict__ x, int words, const uint32_t*
     }
     __syncthreads();
   }
-  merge_ranked<K>(warp_keys, NW * K, out_keys);
+  if (warp == 0) {
+    // the warps' sorted lists folded by insertion (after the first list few
+    // keys pass the threshold)
+    entry = 0;
+    thr = 0;
+    for (int base = 0; base < NW * K; base += 32) {
+      unsigned long long key = (base + lane < NW * K) ? warp_keys[base + lane] : 0ull;
+      list_offer<K>(entry, thr, key, lane);
+    }
+    if (lane < K) out_keys[lane] = entry;
+  }
+  __syncthreads();
 }
 
 // The draw and top-k/top-p of one row (fp32_sse2.rs:1818-1845, inference.rs:
