@@ -116,52 +116,6 @@ __device__ void norm_row_warp(const float* __restrict__ x, const float* __restri
   }
 }
 
-// Phase 1: the B block dots and terms of every (row, block) of `rows` weight
-// rows in shared memory, into terms[(s * rows + r) * (nb + 1) + block].
-template <int BPB>
-__device__ __forceinline__ void block_terms(const uint8_t* ws, int rows_cta, int nb, int cols, int B,
-                                            const int8_t* aq_s, const float* ad_s,
-                                            const int* asum_s, float* terms) {
-  const int tid = threadIdx.x;
-  const size_t row_bytes = (size_t)nb * BPB;
-  const int tstride = nb + 1;
-  for (int item = tid; item < rows_cta * nb; item += kSgThreads) {
-    const int r = item / nb, blk = item - r * nb;
-    const uint8_t* bp = ws + (size_t)r * row_bytes + (size_t)blk * BPB;
-    const float dW = half_to_f32(*reinterpret_cast<const uint16_t*>(bp));
-    uint32_t wq[8];
-    if (BPB == 18) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t p = ld_u32_2aligned_s(bp + 2 + 4 * j);
-        wq[j] = p & 0x0f0f0f0fu;
-        wq[4 + j] = (p >> 4) & 0x0f0f0f0fu;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) wq[j] = ld_u32_2aligned_s(bp + 2 + 4 * j);
-    }
-    for (int s = 0; s < B; ++s) {
-      const uint4* ap = reinterpret_cast<const uint4*>(aq_s + (size_t)s * cols + blk * 32);
-      const uint4 a0 = ap[0], a1 = ap[1];
-      const int aw[8] = {(int)a0.x, (int)a0.y, (int)a0.z, (int)a0.w,
-                         (int)a1.x, (int)a1.y, (int)a1.z, (int)a1.w};
-      int dot = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) dot = __dp4a((int)wq[j], aw[j], dot);
-      const float dA = ad_s[s * nb + blk];
-      float term;
-      if (BPB == 18) {
-        dot -= 8 * asum_s[s * nb + blk];
-        term = __fmul_rn(__fmul_rn(__int2float_rn(dot), dW), dA);
-      } else {
-        term = __fmul_rn(__int2float_rn(dot), __fmul_rn(dW, dA));
-      }
-      terms[((size_t)s * rows_cta + r) * tstride + blk] = term;
-    }
-  }
-}
-
 template <int BPB>
 __global__ void __launch_bounds__(kSgThreads)
 small_gemv_kernel(SmallGemv g, Batch b, unsigned int* status) {
@@ -287,7 +241,41 @@ small_gemv_kernel(SmallGemv g, Batch b, unsigned int* status) {
   }
 
   // ---- phase 1: block dots and terms of every (row, block)
-  block_terms<BPB>(ws, rows_cta, nb, g.cols, B, aq_s, ad_s, asum_s, terms);
+  for (int item = tid; item < rows_cta * nb; item += kSgThreads) {
+    const int r = item / nb, blk = item - r * nb;
+    const uint8_t* bp = ws + (size_t)r * row_bytes + (size_t)blk * BPB;
+    const float dW = half_to_f32(*reinterpret_cast<const uint16_t*>(bp));
+    uint32_t wq[8];
+    if (BPB == 18) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t p = ld_u32_2aligned_s(bp + 2 + 4 * j);
+        wq[j] = p & 0x0f0f0f0fu;
+        wq[4 + j] = (p >> 4) & 0x0f0f0f0fu;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wq[j] = ld_u32_2aligned_s(bp + 2 + 4 * j);
+    }
+    for (int s = 0; s < B; ++s) {
+      const uint4* ap = reinterpret_cast<const uint4*>(aq_s + (size_t)s * g.cols + blk * 32);
+      const uint4 a0 = ap[0], a1 = ap[1];
+      const int aw[8] = {(int)a0.x, (int)a0.y, (int)a0.z, (int)a0.w,
+                         (int)a1.x, (int)a1.y, (int)a1.z, (int)a1.w};
+      int dot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dot = __dp4a((int)wq[j], aw[j], dot);
+      const float dA = ad_s[s * nb + blk];
+      float term;
+      if (BPB == 18) {
+        dot -= 8 * asum_s[s * nb + blk];
+        term = __fmul_rn(__fmul_rn(__int2float_rn(dot), dW), dA);
+      } else {
+        term = __fmul_rn(__int2float_rn(dot), __fmul_rn(dW, dA));
+      }
+      terms[((size_t)s * rows_cta + r) * tstride + blk] = term;
+    }
+  }
   __syncthreads();
 
   // ---- phase 2: the ordered sums and the epilogue
@@ -332,123 +320,6 @@ small_gemv_kernel(SmallGemv g, Batch b, unsigned int* status) {
   }
 }
 
-__device__ __forceinline__ bool sg_wait(uint64_t* bar, uint32_t parity, uint64_t ns) {
-  const uint64_t deadline = sg_ns() + ns;
-  for (;;) {
-    uint32_t ok = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 20000;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(sg_smem(bar)), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if (sg_ns() > deadline) return false;
-  }
-}
-
-// One matrix with many row tiles (the output heads): persistent CTAs, tile
-// i, i + G, ... of rt rows each, whose weights stream through two shared-
-// memory stages by bulk copy (the next tile's copy runs while this one is
-// computed), then the same phases as small_gemv_kernel with the store
-// epilogue.  Every wait is bounded (200 ms; then *status is set, the copies in
-// flight are waited for, bounded again, and the CTA returns).
-template <int BPB>
-__global__ void __launch_bounds__(kSgThreads)
-small_gemv_stream_kernel(SmallGemv g, Batch b, unsigned int* status) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  pdl_trigger();
-  const int tid = threadIdx.x;
-  const int nb = g.cols / 32;
-  const size_t row_bytes = (size_t)nb * BPB;
-  const int B = b.rows;
-  const int tiles = g.seg[0].rows_end / g.rt;
-  const uint32_t tile_bytes = (uint32_t)(g.rt * row_bytes);
-  const size_t stage_bytes = ((size_t)tile_bytes + 127) & ~(size_t)127;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [2]
-  uint8_t* ws = smem + 128;
-  int8_t* aq_s = reinterpret_cast<int8_t*>(ws + 2 * stage_bytes);
-  float* ad_s = reinterpret_cast<float*>(aq_s + (size_t)B * g.cols);
-  int* asum_s = reinterpret_cast<int*>(ad_s + B * nb);
-  float* terms = reinterpret_cast<float*>(asum_s + B * nb);
-  const int tstride = nb + 1;
-  const int G = gridDim.x;
-
-  auto issue = [&](int tile, int st) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sg_smem(&bar[st])),
-                 "r"(tile_bytes)
-                 : "memory");
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            sg_smem(ws + st * stage_bytes)),
-        "l"(g.seg[0].w + (size_t)tile * g.rt * row_bytes), "r"(tile_bytes), "r"(sg_smem(&bar[st]))
-        : "memory");
-  };
-  if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sg_smem(&bar[0])) : "memory");
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sg_smem(&bar[1])) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  if (tid == 0) {
-    if ((int)blockIdx.x < tiles) issue(blockIdx.x, 0);
-    if ((int)blockIdx.x + G < tiles) issue(blockIdx.x + G, 1);
-  }
-  pdl_wait();
-  {
-    const int chunks = g.cols / 16;
-    for (int i = tid; i < B * chunks; i += kSgThreads) {
-      const int s = i / chunks, c = i % chunks;
-      reinterpret_cast<uint4*>(aq_s + (size_t)s * g.cols)[c] =
-          reinterpret_cast<const uint4*>(b.aq + (size_t)s * kActStride)[c];
-    }
-    for (int i = tid; i < B * nb; i += kSgThreads) {
-      const int s = i / nb, k = i % nb;
-      ad_s[i] = b.ad[(size_t)s * kActBlocks + k];
-      asum_s[i] = b.asum[(size_t)s * kActBlocks + k];
-    }
-  }
-  __syncthreads();
-  const Epilogue& ep = g.seg[0].ep;
-  int k = 0;
-  for (int tile = blockIdx.x; tile < tiles; tile += G, ++k) {
-    const int st = k & 1;
-    const bool landed = sg_wait(&bar[st], (uint32_t)(k >> 1) & 1u, 200000000ull);
-    if (!__syncthreads_and(landed)) {
-      if (tid == 0) {
-        atomicOr(status, 1u);
-        // the copies still in flight: this tile's and the next one's
-        sg_wait(&bar[st], (uint32_t)(k >> 1) & 1u, 50000000ull);
-        if (tile + G < tiles) sg_wait(&bar[st ^ 1], (uint32_t)((k + 1) >> 1) & 1u, 50000000ull);
-      }
-      __syncthreads();
-      return;
-    }
-    block_terms<BPB>(ws + st * stage_bytes, g.rt, nb, g.cols, B, aq_s, ad_s, asum_s, terms);
-    __syncthreads();  // the stage is consumed: refill it with tile + 2G
-    if (tid == 0 && tile + 2 * G < tiles) issue(tile + 2 * G, st);
-    const int r0 = tile * g.rt;
-    for (int item = tid; item < B * g.rt; item += kSgThreads) {
-      const int s = item / g.rt, r = item - s * g.rt;
-      const float* t = terms + ((size_t)s * g.rt + r) * tstride;
-      float acc = 0.0f;
-      for (int q = 0; q < nb; ++q) acc = __fadd_rn(acc, t[q]);
-      const int orow = r0 + r;
-      ep.out[(size_t)s * ep.ld + orow] = acc;
-      check_finite(acc, &ep.err[s], ep.layer_ordinal, ep.domain, 0, orow);
-    }
-    __syncthreads();  // terms are rewritten by the next tile
-  }
-}
-
-size_t small_gemv_stream_smem(const SmallGemv& g, int B) {
-  const int nb = g.cols / 32;
-  const int bpb = g.wtype == W_Q4_0 ? 18 : 34;
-  const size_t stage = (((size_t)g.rt * nb * bpb) + 127) & ~(size_t)127;
-  return 128 + 2 * stage + (size_t)B * g.cols + (size_t)B * nb * 8 + (size_t)B * g.rt * (nb + 1) * 4;
-}
-
 size_t small_gemv_smem(const SmallGemv& g, int B) {
   const int nb = g.cols / 32;
   const int bpb = g.wtype == W_Q4_0 ? 18 : 34;
@@ -483,30 +354,10 @@ void launch_small_gemv(const SmallGemv& g, const Batch& b, unsigned int* status,
   if (attribute_needed(configured)) {
     cudaFuncSetAttribute(small_gemv_kernel<18>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(small_gemv_kernel<34>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    cudaFuncSetAttribute(small_gemv_stream_kernel<18>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         200 * 1024);
-    cudaFuncSetAttribute(small_gemv_stream_kernel<34>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         200 * 1024);
     attribute_done(configured);
   }
   const int rows = g.swiglu ? g.seg[0].rows_end : g.seg[g.nseg - 1].rows_end;
   const int grid = rows / g.rt;
-  int sms = 148;
-  {
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  }
-  if (g.nseg == 1 && !g.swiglu && !g.norm_weight && g.seg[0].ep.mode == EPI_STORE &&
-      grid >= 8 * sms && small_gemv_stream_smem(g, b.rows) <= 110 * 1024) {
-    // many tiles of one matrix: persistent CTAs, two per SM, double-buffered
-    const int pgrid = std::min(grid, 2 * sms);
-    const size_t smem = small_gemv_stream_smem(g, b.rows);
-    if (g.wtype == W_Q4_0)
-      launch_pdl(small_gemv_stream_kernel<18>, pgrid, kSgThreads, smem, s, g, b, status);
-    else
-      launch_pdl(small_gemv_stream_kernel<34>, pgrid, kSgThreads, smem, s, g, b, status);
-    return;
-  }
   const size_t smem = small_gemv_smem(g, b.rows);
   if (g.wtype == W_Q4_0)
     launch_pdl(small_gemv_kernel<18>, grid, kSgThreads, smem, s, g, b, status);
