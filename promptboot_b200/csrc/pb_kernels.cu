@@ -366,8 +366,12 @@ void launch_rope_kv(const Batch& b, int layer, const float* rope, cudaStream_t s
 
 int launch_attention(const Batch& b, int layer, int max_span, bool quantize, const float* rope,
                      cudaStream_t s) {
+  // The grouped path runs one PV block per (row, KV head): at few rows that
+  // leaves most of the 148 SMs idle, and the split path (softmax, then one PV
+  // block per group of output components) is faster up to 64 rows at
+  // 512-1535 positions.  PB_ATTN_SPLIT=0/1 forces either path.
   const char* f = std::getenv("PB_ATTN_SPLIT");
-  const bool split = f && std::atoi(f) != 0;
+  const bool split = f && *f ? std::atoi(f) != 0 : b.rows <= kAttnSplitRows && max_span > kAttnSplitMinSpan;
   if (max_span <= kAttnMaxPositions && !split)
     return launch_attention_grouped(b, layer, (max_span + 3) & ~3, quantize, rope, s);
   return launch_attention_long(b, layer, (max_span + 3) & ~3, quantize, rope, s);

@@ -88,6 +88,10 @@ struct Batch {
 // Longest softmax span the shared-memory attention path holds; longer contexts
 // keep the probabilities in the global score scratch.
 constexpr int kAttnMaxPositions = 2048;
+// Batches of at most kAttnSplitRows rows over more than kAttnSplitMinSpan
+// positions take the split (global-scratch) path at any span.
+constexpr int kAttnSplitRows = 64;
+constexpr int kAttnSplitMinSpan = 256;
 
 enum EpiMode : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
 

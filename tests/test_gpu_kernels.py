@@ -155,8 +155,12 @@ def test_rope_and_kv_write_match_fixture_and_oracle():
                 assert gkv[base + vw] == v[r, h * 64 + c]
 
 
+@pytest.mark.parametrize("path", ["0", "1"])
 @pytest.mark.parametrize("current,span,fixture,rot", [(2, 256, "256", 0), (256, 512, "512", 7)])
-def test_attention_matches_fixtures(current, span, fixture, rot):
+def test_attention_matches_fixtures(monkeypatch, current, span, fixture, rot, path):
+    """The reference's attention fixtures through the grouped (0) and the split
+    (1) launches."""
+    monkeypatch.setenv("PB_ATTN_SPLIT", path)
     lib = _lib.load()
     cap = 32768
     kv = attention_fixture_kv(cap)
@@ -177,10 +181,13 @@ def test_attention_matches_fixtures(current, span, fixture, rot):
                                           ([29, 255, 256], 1024), ([511, 512, 600], 1024),
                                           ([63, 64, 65], 1024), ([1023, 2046, 2047], 2048),
                                           ([2048, 2100, 1], 2560)])
-def test_attention_random_kv_matches_oracle(positions, cap):
+@pytest.mark.parametrize("path", ["0", "1"])
+def test_attention_random_kv_matches_oracle(monkeypatch, positions, cap, path):
     """Edge spans (1..N positions, masked tails, tile boundaries at 64), the
-    shared-memory path up to 2048 positions and the global-scores path beyond,
+    shared-memory path up to 2048 positions (forced with PB_ATTN_SPLIT=0) and
+    the global-scores path (forced with 1, and taken beyond 2048 either way),
     and the reference's denormal / signed-zero query words (tests.rs:699-706)."""
+    monkeypatch.setenv("PB_ATTN_SPLIT", path)
     lib = _lib.load()
     rows = len(positions)
     rng = np.random.default_rng(sum(positions))
