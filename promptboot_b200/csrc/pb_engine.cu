@@ -187,7 +187,9 @@ struct pb_engine {
   // Graphs pay where the host's launch rate bounds a step: small batches.  A
   // large batch's step is bound by the GPU, and a capture (~ms) would fall
   // into whichever step first repeats a key.
-  static constexpr uint32_t kGraphMaxRows = 16;
+  static constexpr uint32_t kGraphMaxRows = 64;
+  // Span bucket of the graph key: one capture per kGraphSpanBucket positions.
+  static constexpr int kGraphSpanBucket = 128;
 
   // pinned host staging
   int *h_slots = nullptr, *h_positions = nullptr;
@@ -395,10 +397,13 @@ struct pb_engine {
     return cudaGraphLaunch(entry->exec, stream) == cudaSuccess;
   }
 
-  // The softmax span rounded for the graph key (64 positions; the grouped
-  // path's limit is a multiple of 64, so the choice of path is unchanged).
+  // The softmax span rounded up for the graph key.  The kernels bound their
+  // work by each row's own position, and the attention path is chosen from
+  // (rows, rounded span), so every replay of a key takes the same launches.
   int graph_span(int span, uint32_t rows) const {
-    return graphs_enabled && rows <= kGraphMaxRows ? (span + 63) & ~63 : span;
+    return graphs_enabled && rows <= kGraphMaxRows
+               ? (span + kGraphSpanBucket - 1) / kGraphSpanBucket * kGraphSpanBucket
+               : span;
   }
 
   // Small batches: gate and up rows of one 32-row block per CTA, SwiGLU and the
@@ -1187,13 +1192,22 @@ uint32_t pb_engine_generate(pb_engine* e, uint32_t n, const uint32_t* seqs,
         pb::launch_pdl(take_sample_kernel, blocks, threads, 0, e->stream, e->d_sampled,
                        e->d_tokens, e->d_positions, e->d_base, e->d_samp_status, e->d_token_log,
                        (int)n);
-        e->enqueue_forward(n, true, e->d_err_cur, greedy);
+        e->enqueue_forward(n, true, e->d_err_cur, false);
         pb::launch_pdl(finish_step_kernel, blocks, threads, 0, e->stream, e->d_positions, e->d_base,
                        e->d_err_cur, e->d_err, (int)n);
         e->launches += 3;
       };
-      if (!e->run_step(pb_engine::GraphKey{n, e->max_span, greedy ? 2 : 1}, one_step))
+      // The last step's greedy id comes from a launch of its own, so that
+      // every step of a generate call replays the same graph.
+      if (!e->run_step(pb_engine::GraphKey{n, e->max_span, 1}, one_step))
         PB_CUDA(cudaGetLastError());
+      if (greedy) {
+        e->prof_mark(PB_KC_ARGMAX);
+        pb::launch_argmax(e->logits, pb::kVocab, (int)n, pb::kVocab, e->d_greedy,
+                          e->d_greedy_bits, nullptr, e->stream);
+        e->prof_mark(PB_KC_ARGMAX);
+        ++e->launches;
+      }
     }
     PB_CUDA(cudaGetLastError());
     std::vector<unsigned long long> serr((size_t)chunk * n);
