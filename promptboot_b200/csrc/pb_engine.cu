@@ -188,6 +188,10 @@ struct pb_engine {
   // large batch's step is bound by the GPU, and a capture (~ms) would fall
   // into whichever step first repeats a key.
   static constexpr uint32_t kGraphMaxRows = 64;
+  // Graphs of steps of at most this many rows are captured without
+  // programmatic dependent launch: measured 3-12% faster per step at 1-32 rows
+  // (and 4.7% slower at 64), while PDL pays in stream-launched steps.
+  static constexpr uint32_t kGraphNoPdlRows = 32;
   // Span bucket of the graph key: one capture per kGraphSpanBucket positions.
   static constexpr int kGraphSpanBucket = 128;
 
@@ -377,7 +381,10 @@ struct pb_engine {
         enqueue();
         return true;
       }
-      enqueue();
+      {
+        pb::PdlOff off(key.rows <= kGraphNoPdlRows);
+        enqueue();
+      }
       cudaGraph_t graph = nullptr;
       cudaError_t e = cudaStreamEndCapture(stream, &graph);
       if (e == cudaSuccess) e = cudaGraphInstantiate(&entry->exec, graph, 0);

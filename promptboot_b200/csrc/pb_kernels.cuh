@@ -25,6 +25,16 @@ inline void attribute_done(std::atomic<uint64_t>& done) {
   if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) done.fetch_or(1ull << dev);
 }
 
+// Whether this host thread's launch_pdl calls ask for programmatic
+// serialization (PdlOff turns it off for a scope; the kernels' griddepcontrol
+// instructions are then no-ops).
+inline thread_local bool t_pdl_enabled = true;
+struct PdlOff {
+  bool saved;
+  explicit PdlOff(bool off) : saved(t_pdl_enabled) { if (off) t_pdl_enabled = false; }
+  ~PdlOff() { t_pdl_enabled = saved; }
+};
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                               cudaStream_t s, Args... args) {
@@ -37,7 +47,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = t_pdl_enabled ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
