@@ -184,10 +184,10 @@ struct pb_engine {
   uint64_t graph_clock = 0;
   bool graphs_enabled = true;
   static constexpr size_t kMaxGraphs = 16;
-  // Graphs pay where the host's launch rate bounds a step: small batches.  A
-  // large batch's step is bound by the GPU, and a capture (~ms) would fall
-  // into whichever step first repeats a key.
-  static constexpr uint32_t kGraphMaxRows = 64;
+  // Steps of up to this many rows replay graphs: measured +1% per step at 256
+  // rows, +3% at 128 and more below; a key's capture (~ms) falls into the
+  // second step of each span bucket, once per 128 positions.
+  static constexpr uint32_t kGraphMaxRows = 256;
   // Graphs of steps of at most this many rows are captured without
   // programmatic dependent launch: measured 3-12% faster per step at 1-32 rows
   // (and 4.7% slower at 64), while PDL pays in stream-launched steps.
