@@ -379,7 +379,7 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
 
 template <int G, bool kScaled, bool kCheckV>
 __global__ void __launch_bounds__(PvChains<G>::kThreads)
-attention_pv_chains_kernel(Batch b, int layer) {
+attention_pv_chains_kernel(Batch b, int layer, bool quantize) {
   using C = PvChains<G>;
   pdl_begin();
   extern __shared__ __align__(16) float sm[];
@@ -498,6 +498,9 @@ attention_pv_chains_kernel(Batch b, int layer) {
   const int qh_index = kh * kHeadsPerKv + h;
   b.attn[(size_t)row * kHidden + qh_index * 64 + comp] = o;
   check_finite(o, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + comp);
+  // Two groups: warp h holds the 32 outputs of Q8_0 block 2 qh + grp of the
+  // o-projection input, element = lane.
+  if (G == 2 && quantize) quantize_row_block(b, o, row, 2 * qh_index + grp);
 }
 
 // Scores over chunks of 128 positions: lane l of warp h takes the 4-position K
@@ -633,7 +636,7 @@ constexpr size_t kScores4Smem = (size_t)(kChunk4 / 4) * kTilePitch * 4;
 int attention_smem_positions() { return kAttnMaxPositions; }
 
 template <int G, bool kScaled, bool kCheckV>
-static void launch_pv_chains_as(const Batch& b, int layer, cudaStream_t s) {
+static void launch_pv_chains_as(const Batch& b, int layer, bool quantize, cudaStream_t s) {
   using C = PvChains<G>;
   static std::atomic<uint64_t> configured{0};
   if (attribute_needed(configured)) {
@@ -642,13 +645,13 @@ static void launch_pv_chains_as(const Batch& b, int layer, cudaStream_t s) {
     attribute_done(configured);
   }
   launch_pdl(attention_pv_chains_kernel<G, kScaled, kCheckV>, dim3(b.rows * 2, G), C::kThreads,
-             C::kBytes, s, b, layer);
+             C::kBytes, s, b, layer, quantize);
 }
 
 template <int G>
-static void launch_pv_chains(const Batch& b, int layer, cudaStream_t s) {
-  if (b.kv_checked) launch_pv_chains_as<G, true, false>(b, layer, s);
-  else launch_pv_chains_as<G, true, true>(b, layer, s);
+static void launch_pv_chains(const Batch& b, int layer, bool quantize, cudaStream_t s) {
+  if (b.kv_checked) launch_pv_chains_as<G, true, false>(b, layer, quantize, s);
+  else launch_pv_chains_as<G, true, true>(b, layer, quantize, s);
 }
 
 static void configure_scores4() {
@@ -683,14 +686,18 @@ int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quant
   return 2;
 }
 
-// Component groups of the long-context PV launch (PB_ATTN_LONG_GROUPS=4|8|16
-// in the environment selects one for tuning sweeps; tests cover each).
-int attention_long_groups() {
+// Component groups of the split PV launch: two (224 threads, warp = query
+// head, the launch then quantizes its own output for the o projection) from 16
+// rows, where that saves a launch (32 rows: 13.3k against 12.6k tok/s per
+// step); four below, where the CTA count is short (8 rows at 30,000 positions:
+// 614 against 537 tok/s).  PB_ATTN_LONG_GROUPS=2|4|8|16 in the environment
+// selects one for tuning sweeps; tests cover each.
+int attention_long_groups(int rows) {
   if (const char* f = std::getenv("PB_ATTN_LONG_GROUPS")) {
     const int g = std::atoi(f);
-    if (g == 4 || g == 8 || g == 16) return g;
+    if (g == 2 || g == 4 || g == 8 || g == 16) return g;
   }
-  return 4;
+  return rows >= 16 ? 2 : 4;
 }
 
 int launch_attention_long(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
@@ -700,10 +707,15 @@ int launch_attention_long(const Batch& b, int layer, int span_cap, bool quantize
   launch_pdl(attention_scores4_kernel, dim3(chunks, b.rows * 2), kThreads, kScores4Smem, s, b, layer,
              rope);
   launch_pdl(attention_softmax_long_kernel, b.rows * kQHeads, kLongThreads, 0, s, b);
-  const int groups = attention_long_groups();
-  if (groups == 4) launch_pv_chains<4>(b, layer, s);
-  else if (groups == 16) launch_pv_chains<16>(b, layer, s);
-  else launch_pv_chains<8>(b, layer, s);
+  const int groups = attention_long_groups(b.rows);
+  if (groups == 2) {
+    // the PV launch quantizes its own output
+    launch_pv_chains<2>(b, layer, quantize, s);
+    return 3;
+  }
+  if (groups == 4) launch_pv_chains<4>(b, layer, false, s);
+  else if (groups == 16) launch_pv_chains<16>(b, layer, false, s);
+  else launch_pv_chains<8>(b, layer, false, s);
   if (quantize) {
     launch_quant(b, b.attn, kHidden, kHidden, s);
     return 4;

@@ -12,7 +12,8 @@ inference.rs:914-965 / fp32_sse2.rs:1787-1876.
   width live together), checked against the oracle on a spread of rows;
 * the engine past the 2,048 positions of the shared-memory attention path, at
   2,100 prefilled positions and at config 4's ~31,000 positions over a seeded
-  KV cache restored into a slot.
+  KV cache restored into a slot;
+* the split attention launches of a 20-sequence batch past 256 positions.
 """
 from __future__ import annotations
 
@@ -209,6 +210,30 @@ def test_engine_restored_long_context_matches_oracle(model_view, model_image):
     assert np.array_equal(_kv_positions(got, cap, [n, n + 1]).view(np.uint32),
                           _kv_positions(kv, cap, [n, n + 1]).view(np.uint32))
     eng.close()
+
+
+def test_engine_split_attention_batch_matches_oracle(model_view, model_image):
+    """20 sequences past 256 positions: the engine's decode step takes the split
+    attention launches (scores, softmax, the two-group PV launch that also
+    quantizes the o-projection input); rows 0, 9 and 19 against oracle
+    forwards over the engine's own KV, logits bit for bit."""
+    n, plen, cap = 20, 300, 320
+    prompts = np.stack([shard.prompt_for(200 + s, plen) for s in range(n)])
+    eng = api.InferenceEngine(model_view, max_seqs=n, max_context=cap)
+    status, _, errs = eng.prefill_batch(np.arange(n), prompts, 8)
+    assert status == 0
+    torch.cuda.synchronize()
+    rows = [0, 9, 19]
+    kvs = {r: eng.kv_tensor(r).cpu().numpy().copy() for r in rows}
+    tokens = np.array([(1000 + 37 * s) % 151936 for s in range(n)], dtype=np.uint32)
+    status, _, errs = eng.decode_batch(np.arange(n), tokens, require_greedy=False)
+    assert status == 0
+    got = {r: eng.logits(r) for r in rows}
+    eng.close()
+    for r in rows:
+        st, ref, _ = oracle.forward(model_image, kvs[r], cap, int(tokens[r]), plen, True)
+        assert st == 0
+        assert np.array_equal(got[r], ref.view(np.uint32)), r
 
 
 def test_sampler_expf_matches_reference_edges_and_dense_sweep():

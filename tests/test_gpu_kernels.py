@@ -282,7 +282,7 @@ def test_attention_extreme_magnitudes_match_oracle(case):
         assert _same_bits_or_nan(got[r], ref), (case, r, positions[r])
 
 
-@pytest.mark.parametrize("groups", ["4", "8", "16"])
+@pytest.mark.parametrize("groups", ["2", "4", "8", "16"])
 @pytest.mark.parametrize("case", ["random", "wide_scores", "overflowing_products", "inf_value",
                                   "nan_key", "tiny_values", "wide_values"])
 def test_attention_long_context_extremes_match_oracle(monkeypatch, case, groups):
