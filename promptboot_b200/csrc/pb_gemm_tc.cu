@@ -235,8 +235,9 @@ struct TcCfg {
   // TMEM groups of 4 block dots: the MMA runs up to kGroups - 1 chunks ahead of
   // the epilogue, hiding the MMA issue-to-commit latency.
   static constexpr int kGroups = GROUPS_;
-  // Q-blocks per TMEM load batch (32 registers of block dots per thread).
-  static constexpr int kBatch = kCpw * kKC <= 16 ? kKC : 2;
+  // Q-blocks per TMEM load batch (up to 32 registers of block dots per thread:
+  // the whole chunk, one load wait, for 8-column epilogue warps).
+  static constexpr int kBatch = kCpw * kKC <= 32 ? kKC : 2;
   static constexpr int kBOff = kTcChunkBytes;  // [NT/8] groups of kTcGroupBytes
   static constexpr int kStage = kBOff + (NT / 8) * kTcGroupBytes;
   static constexpr uint32_t kTxBytes = kTcChunkBytes + (SEQ / 8) * kTcGroupBytes;  // per chunk
