@@ -169,7 +169,7 @@ struct pb_engine {
   struct GraphKey {
     uint32_t rows;
     int span;
-    int kind;  // 0 decode forward, 1 generate step, 2 generate step + greedy
+    int kind;  // 0 decode forward, 1 generate step (its greedy argmax runs outside the graph)
     bool operator==(const GraphKey& o) const {
       return rows == o.rows && span == o.span && kind == o.kind;
     }

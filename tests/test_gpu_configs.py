@@ -127,9 +127,12 @@ def test_config3_batch_of_256_matches_oracle_on_spread_rows(model_view, model_im
         status, out, errs = eng.generate(np.arange(n), states, steps)
         assert status == 0
         got_logits = {r: eng.logits(r) for r in rows}
+        results = [fut.result() for fut in refs]
+        # the greedy id of the last generate step (launched after the step's
+        # graph) is the one decode continues from
+        eng.decode(oracle.argmax(results[-1][1]), seq=rows[-1])
         eng.close()
-        for r, fut in zip(rows, refs):
-            ids, logits = fut.result()
+        for r, (ids, logits) in zip(rows, results):
             assert list(out[:, r]) == ids, r
             assert np.array_equal(got_logits[r], logits.view(np.uint32)), r
             assert states[r].draws() == steps
