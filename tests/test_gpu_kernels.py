@@ -339,18 +339,20 @@ def test_attention_long_context_extremes_match_oracle(monkeypatch, case, groups)
         assert _same_bits_or_nan(got_p[r, 13, :span], ref_p[:span]), (case, r)
 
 
+@pytest.mark.parametrize("limit", [2300, 2040])
 @pytest.mark.parametrize("case", ["random", "wide_values", "inf_value", "nan_key", "wide_scores"])
-def test_attention_split_path_many_rows_matches_oracle(monkeypatch, case):
-    """The long-context launches (scores, global softmax, one-chain PV) forced
-    for every span at 64 rows, spans from 1 position past 2,048, with the
-    extreme cases that force every fallback (non-finite products in the
-    integer-built score chains, the serial softmax sum)."""
+def test_attention_split_path_many_rows_matches_oracle(monkeypatch, case, limit):
+    """The split launches (scores, global softmax, two-group one-chain PV)
+    forced for every span at 64 rows, spans past 2,048 and up to 2,044, with
+    the extreme cases that force every fallback (non-finite products in the
+    integer-built score chains, the serial softmax sum); the final
+    probabilities too."""
     monkeypatch.setenv("PB_ATTN_SPLIT", "1")
     lib = _lib.load()
-    cap, layer, rows = 2304, 0, 64
-    rng = np.random.default_rng(sum(map(ord, case)))
-    positions = [int(x) for x in rng.integers(0, 2300, rows)]
-    positions[:6] = [0, 1, 2, 3, 127, 2299]
+    cap, layer, rows = (limit + 4) // 4 * 4, 0, 64
+    rng = np.random.default_rng(sum(map(ord, case)) + limit)
+    positions = [int(x) for x in rng.integers(0, limit, rows)]
+    positions[:6] = [0, 1, 2, 3, 127, limit - 1]
     slot = 24 * 4 * cap * 64
     kv_d = torch.zeros(rows * slot, dtype=torch.float32, device="cuda")
     regions = []
@@ -372,17 +374,21 @@ def test_attention_split_path_many_rows_matches_oracle(monkeypatch, case):
         regions.append(kvr)
         kv_d[r * slot:r * slot + kvr.size] = torch.from_numpy(kvr).to("cuda")
     out = torch.zeros((rows, 896), dtype=torch.float32, device="cuda")
+    span_max = max((p + 4) & ~3 for p in positions)
+    probs = torch.zeros((rows, 14, span_max), dtype=torch.float32, device="cuda")
     pos = np.array(positions, dtype=np.uint32)
     assert lib.pb_attention_device(ptr(dev(q)), ptr(kv_d), cap, layer,
-                                   pos.ctypes.data_as(ctypes.c_void_p), rows, 0, ptr(out), None,
+                                   pos.ctypes.data_as(ctypes.c_void_p), rows, 0, ptr(out), ptr(probs),
                                    None) == 0
     sync()
-    got = host(out)
+    got, got_p = host(out), host(probs)
     full = np.zeros(slot, dtype=np.float32)
     for r in range(rows):
         full[:regions[r].size] = regions[r]
-        ref, _ = oracle.attention(q[r], full, cap, layer, positions[r], (positions[r] + 4) & ~3)
+        span = (positions[r] + 4) & ~3
+        ref, ref_p = oracle.attention(q[r], full, cap, layer, positions[r], span)
         assert _same_bits_or_nan(got[r], ref), (case, r, positions[r])
+        assert _same_bits_or_nan(got_p[r, 13, :span], ref_p[:span]), (case, r)
 
 
 def _q4_weights(rng, rows, cols):
