@@ -35,6 +35,7 @@
 #include "pb_quant.cuh"
 
 #include <cstdlib>
+#include <cstring>
 
 namespace pb {
 namespace {
@@ -503,6 +504,199 @@ attention_pv_chains_kernel(Batch b, int layer, bool quantize) {
   if (G == 2 && quantize) quantize_row_block(b, o, row, 2 * qh_index + grp);
 }
 
+// The PV chains for few rows, fed by producer warps.  With at most 8 rows the
+// chains of a step fill at most 128 CTAs of two chain warps, one warp per
+// scheduler, and a chain thread that also forms its products (multiply, three
+// integer operations for the scaled image, the loads) issues ~22 cycles per
+// position against the 8.2-cycle dependent add.  Here the CTA of (sequence, KV
+// head, one of 8 component groups) holds 2 chain warps (the 56 chains: 7 heads
+// x 8 components) and 8 producer warps (four per chain, a quarter of each
+// chunk each), one CTA per SM: the producers stream V (transposed) and the
+// probabilities through kStages
+// cp.async stages and write the scaled f64 images of the products of chunk
+// t + 1 into a shared term buffer ([position pair][chain] double2) while the
+// chain warps add chunk t's terms in position order, two 16-byte loads per
+// four adds.  One barrier per chunk separates the two buffers' roles.
+struct PvFed {
+  static constexpr int kComps = 8;                          // components per CTA
+  static constexpr int kGroups = 64 / kComps;               // grid.y
+  static constexpr int kChains = kHeadsPerKv * kComps;      // 56
+  static constexpr int kSlots = 64;                         // term row pitch (double2)
+  static constexpr int kChainThreads = kSlots;              // warps 0-1
+  static constexpr int kParts = 4;                          // producers per chain
+  static constexpr int kProducers = kParts * kSlots;        // (slot, quarter chunk)
+  static constexpr int kThreads = kChainThreads + kProducers;  // 320
+  static constexpr int kChunk = 128;                        // positions per stage
+  static constexpr int kPartQuads = kChunk / 4 / kParts;    // 4-position quads per producer
+  static constexpr int kPitch = kChunk + 4;                 // words per V / probability row
+  static constexpr int kStages = 4;                         // raw cp.async stages
+  static constexpr int kRawWords = (kComps + kHeadsPerKv) * kPitch;
+  static constexpr int kTermPairs = kChunk / 2;
+  static constexpr int kTermStage = kTermPairs * kSlots;    // double2 per term buffer
+  static constexpr size_t kBytes = 2 * (size_t)kTermStage * 16 + (size_t)kStages * kRawWords * 4;
+};
+static_assert(PvFed::kRawWords * 4 % 16 == 0 && PvFed::kComps * PvFed::kPitch * 4 % 16 == 0,
+              "16-byte cp.async destinations");
+
+template <bool kCheckV>
+__global__ void __launch_bounds__(PvFed::kThreads, 1)
+attention_pv_fed_kernel(Batch b, int layer) {
+  using C = PvFed;
+  pdl_begin();
+  extern __shared__ __align__(16) float sm[];
+  __shared__ int s_bad;
+  double2* terms = reinterpret_cast<double2*>(sm);
+  float* raw = sm + 2 * C::kTermStage * 4;
+  const int row = blockIdx.x >> 1, kh = blockIdx.x & 1, grp = blockIdx.y;
+  const int tid = threadIdx.x;
+  const bool producer = tid >= C::kChainThreads;
+  const int pt = tid - C::kChainThreads;                      // producer index
+  const int slot = producer ? (pt & (C::kSlots - 1)) : tid;   // chain of this thread
+  const int part = producer ? pt / C::kSlots : 0;
+  const bool active = slot < C::kChains;
+  const int h = slot / C::kComps, cc = slot % C::kComps;
+  const int comp = grp * C::kComps + cc;
+  const int positions = b.positions[row] + 1;
+  const size_t cap = b.capacity;
+  const float* kv = b.kv + (size_t)b.slots[row] * (size_t)kLayers * 4 * cap * 64;
+  const float* vbase = kv + (size_t)layer * 4 * cap * 64 + 2 * cap * 64 + (size_t)kh * cap * 64;
+  const float* probs = b.scores + ((size_t)row * kQHeads + kh * kHeadsPerKv) * b.score_stride;
+  const int nchunks = (positions + C::kChunk - 1) / C::kChunk;
+
+  auto load = [&](int t) {  // producers: chunk t into raw stage t % kStages
+    if (t < nchunks) {
+      float* stage = raw + (t % C::kStages) * C::kRawWords;
+      const int p0 = t * C::kChunk;
+      const int rows_here = min(C::kChunk, positions - p0);
+      const float* vsrc = vbase + (size_t)p0 * 64 + grp * C::kComps;
+      for (int i = pt; i < rows_here * C::kComps; i += C::kProducers) {
+        const int r = i / C::kComps, c = i % C::kComps;
+        cp_async4(stage + c * C::kPitch + r, vsrc + r * 64 + c);
+      }
+      // probabilities of the 7 heads, rows_here rounded up to 4 (the scratch
+      // holds the padded span)
+      const int quads = (rows_here + 3) >> 2;
+      float* pst = stage + C::kComps * C::kPitch;
+      for (int i = pt; i < kHeadsPerKv * (C::kChunk / 4); i += C::kProducers) {
+        const int hh = i / (C::kChunk / 4), q = i % (C::kChunk / 4);
+        if (q < quads)
+          cp_async16(pst + hh * C::kPitch + 4 * q, probs + (size_t)hh * b.score_stride + p0 + 4 * q);
+      }
+    }
+    cp_commit();  // one group per chunk, empty past the end
+  };
+  float vchk = 0.0f;
+  auto produce = [&](int t) {  // producers: the images of chunk t's products
+    if (!active) return;
+    const float* stage = raw + (t % C::kStages) * C::kRawWords;
+    const float* vt = stage + cc * C::kPitch;
+    const float* pr = stage + C::kComps * C::kPitch + h * C::kPitch;
+    double2* term = terms + (t & 1) * C::kTermStage + slot;
+    const int rows_here = min(C::kChunk, positions - t * C::kChunk);
+    const int i0 = part * (4 * C::kPartQuads);
+    // A quad past rows_here reads stale words (the pitch covers it); the chains
+    // never add those terms.  Unrolled: the quads' loads issue together.
+#pragma unroll
+    for (int k = 0; k < C::kPartQuads; ++k) {
+      const int i = i0 + 4 * k;
+      if (i < rows_here) {
+        const float4 p4 = *reinterpret_cast<const float4*>(pr + i);
+        const float4 v4 = *reinterpret_cast<const float4*>(vt + i);
+        if (kCheckV) {
+          vchk = __fmaf_rn(v4.x, 0.0f, vchk);
+          if (i + 1 < rows_here) vchk = __fmaf_rn(v4.y, 0.0f, vchk);
+          if (i + 2 < rows_here) vchk = __fmaf_rn(v4.z, 0.0f, vchk);
+          if (i + 3 < rows_here) vchk = __fmaf_rn(v4.w, 0.0f, vchk);
+        }
+        term[(i >> 1) * C::kSlots] =
+            make_double2(scaled_image(__fmul_rn(p4.x, v4.x)), scaled_image(__fmul_rn(p4.y, v4.y)));
+        term[((i >> 1) + 1) * C::kSlots] =
+            make_double2(scaled_image(__fmul_rn(p4.z, v4.z)), scaled_image(__fmul_rn(p4.w, v4.w)));
+      }
+    }
+  };
+  double acc = 0.0;
+  auto consume = [&](int t) {  // chain threads: chunk t's terms in position order
+    const double2* term = terms + (t & 1) * C::kTermStage + slot;
+    const int rows_here = min(C::kChunk, positions - t * C::kChunk);
+    const int pairs = rows_here >> 1;
+    int j = 0;
+    if (pairs >= 8) {
+      // the next four pairs load while the current four are added
+      double2 a[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) a[k] = term[k * C::kSlots];
+      for (j = 4; j + 4 <= pairs; j += 4) {
+        double2 n[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) n[k] = term[(j + k) * C::kSlots];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc += a[k].x;
+          acc += a[k].y;
+          a[k] = n[k];
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc += a[k].x;
+        acc += a[k].y;
+      }
+    }
+    for (; j < pairs; ++j) {
+      const double2 a = term[j * C::kSlots];
+      acc += a.x;
+      acc += a.y;
+    }
+    if (rows_here & 1) acc += term[pairs * C::kSlots].x;
+  };
+
+  if (tid == 0) s_bad = 0;
+  if (producer) {
+    load(0);
+    load(1);
+    load(2);
+    asm volatile("cp.async.wait_group 2;" ::: "memory");  // chunk 0 landed (own copies)
+  }
+  __syncthreads();
+  if (producer) {
+    produce(0);
+    cp_wait1();  // chunk 1
+  }
+  __syncthreads();
+  for (int t = 0; t < nchunks; ++t) {
+    if (producer) {
+      load(t + 3);  // into the stage chunk t - 1 held (read two barriers ago)
+      if (t + 1 < nchunks) produce(t + 1);
+      cp_wait1();   // chunk t + 2, for the next iteration
+    } else if (active) {
+      consume(t);
+    }
+    __syncthreads();
+  }
+  if (producer) {
+    cp_wait0();
+    if (kCheckV && vchk != 0.0f) s_bad = 1;
+  }
+  __syncthreads();
+  if (producer || !active) return;
+  // The images need finite products: finite probabilities (position 0's word
+  // shows a non-finite normalizer) and finite V; otherwise the chain is redone
+  // with conversions.
+  const float* hprobs = probs + (size_t)h * b.score_stride;
+  if (fabsf(hprobs[0]) <= 0x1.fffffep127f && s_bad == 0) {
+    acc *= 0x1p896;
+  } else {
+    acc = 0.0;
+    for (int p = 0; p < positions; ++p)
+      acc += (double)__fmul_rn(hprobs[p], vbase[(size_t)p * 64 + comp]);
+  }
+  const float o = (float)acc;
+  const int qh_index = kh * kHeadsPerKv + h;
+  b.attn[(size_t)row * kHidden + qh_index * 64 + comp] = o;
+  check_finite(o, &b.err[row], (uint32_t)layer + 1, D_ATTENTION, 0, qh_index * 64 + comp);
+}
+
 // Scores over chunks of 128 positions: lane l of warp h takes the 4-position K
 // tile l, so one 16-byte shared load serves 4 products, and keeps 4 f64
 // chains: positions 0-1 of the tile convert their products on the XU pipe,
@@ -686,18 +880,36 @@ int launch_attention_grouped(const Batch& b, int layer, int span_cap, bool quant
   return 2;
 }
 
-// Component groups of the split PV launch: two (224 threads, warp = query
-// head, the launch then quantizes its own output for the o projection) from 16
-// rows, where that saves a launch (32 rows: 13.3k against 12.6k tok/s per
-// step); four below, where the CTA count is short (8 rows at 30,000 positions:
-// 614 against 537 tok/s).  PB_ATTN_LONG_GROUPS=2|4|8|16 in the environment
-// selects one for tuning sweeps; tests cover each.
+template <bool kCheckV>
+static void launch_pv_fed_as(const Batch& b, int layer, cudaStream_t s) {
+  static std::atomic<uint64_t> configured{0};
+  if (attribute_needed(configured)) {
+    cudaFuncSetAttribute(attention_pv_fed_kernel<kCheckV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)PvFed::kBytes);
+    attribute_done(configured);
+  }
+  launch_pdl(attention_pv_fed_kernel<kCheckV>, dim3(b.rows * 2, PvFed::kGroups), PvFed::kThreads,
+             PvFed::kBytes, s, b, layer);
+}
+
+// Rows up to which the split PV launch is the producer-fed one (one CTA per SM
+// at most; more CTAs share the shared-memory bandwidth that the term buffer
+// already uses at ~8 bytes a cycle per chain).
+constexpr int kPvFedRows = 8;
+
+// The split PV launch: the producer-fed chains (returned as 0) up to
+// kPvFedRows rows; from 16 rows two component groups (224 threads, warp =
+// query head, the launch then quantizes its own output for the o projection:
+// 32 rows 13.3k against 12.6k tok/s per step); four between.
+// PB_ATTN_LONG_GROUPS=fed|2|4|8|16 in the environment selects one for tuning
+// sweeps; tests cover each.
 int attention_long_groups(int rows) {
   if (const char* f = std::getenv("PB_ATTN_LONG_GROUPS")) {
+    if (std::strcmp(f, "fed") == 0) return 0;
     const int g = std::atoi(f);
     if (g == 2 || g == 4 || g == 8 || g == 16) return g;
   }
-  return rows >= 16 ? 2 : 4;
+  return rows <= kPvFedRows ? 0 : rows >= 16 ? 2 : 4;
 }
 
 int launch_attention_long(const Batch& b, int layer, int span_cap, bool quantize, const float* rope,
@@ -713,7 +925,10 @@ int launch_attention_long(const Batch& b, int layer, int span_cap, bool quantize
     launch_pv_chains<2>(b, layer, quantize, s);
     return 3;
   }
-  if (groups == 4) launch_pv_chains<4>(b, layer, false, s);
+  if (groups == 0) {
+    if (b.kv_checked) launch_pv_fed_as<false>(b, layer, s);
+    else launch_pv_fed_as<true>(b, layer, s);
+  } else if (groups == 4) launch_pv_chains<4>(b, layer, false, s);
   else if (groups == 16) launch_pv_chains<16>(b, layer, false, s);
   else launch_pv_chains<8>(b, layer, false, s);
   if (quantize) {

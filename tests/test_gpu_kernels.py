@@ -282,13 +282,14 @@ def test_attention_extreme_magnitudes_match_oracle(case):
         assert _same_bits_or_nan(got[r], ref), (case, r, positions[r])
 
 
-@pytest.mark.parametrize("groups", ["2", "4", "8", "16"])
+@pytest.mark.parametrize("groups", ["fed", "2", "4", "8", "16"])
 @pytest.mark.parametrize("case", ["random", "wide_scores", "overflowing_products", "inf_value",
                                   "nan_key", "tiny_values", "wide_values"])
 def test_attention_long_context_extremes_match_oracle(monkeypatch, case, groups):
     """The long-context path (probabilities in the global scratch, the softmax
-    sum as an exact tree or its serial fallback, PV chains split into 4, 8 or 16
-    component groups) against the oracle, probabilities included: random K/V
+    sum as an exact tree or its serial fallback, PV chains split into 2, 4, 8 or
+    16 component groups, or fed by producer warps) against the oracle,
+    probabilities included: random K/V
     (the tree sum holds), scores spread over ~200 units (subnormal
     exponentials: the serial fallback), and the non-finite and extreme cases of
     the grouped kernels."""
@@ -297,7 +298,7 @@ def test_attention_long_context_extremes_match_oracle(monkeypatch, case, groups)
     cap, layer = 3008, 0
     positions = [2100, 3000]
     rows = len(positions)
-    rng = np.random.default_rng(sum(map(ord, case)) + int(groups))
+    rng = np.random.default_rng(sum(map(ord, case)) + sum(map(ord, groups)))
     slot = 24 * 4 * cap * 64
     kv = np.zeros(rows * slot, dtype=np.float32)
     q = rng.standard_normal((rows, 896)).astype(np.float32)
