@@ -586,64 +586,83 @@ attention_pv_fed_kernel(Batch b, int layer) {
     cp_commit();  // one group per chunk, empty past the end
   };
   float vchk = 0.0f;
+  // The low and high words of the scaled f64 image of fl(p * v) (the
+  // arithmetic of scaled_image, written out so the words go straight into the
+  // registers of a 16-byte store).
+  auto image = [](float p, float v, uint32_t& lo, uint32_t& hi) {
+    const uint32_t u = __float_as_uint(__fmul_rn(p, v));
+    hi = (uint32_t)((int32_t)u >> 3) & 0x8FFFFFFFu;
+    lo = u << 29;
+  };
+  // One quad of positions: the terms of pairs dst[0] and dst[kSlots]; `valid`
+  // of its positions are below rows_here (the V check covers only those).
+  auto quad = [&](uint4* dst, const float* pq, const float* vq, int valid) {
+    const float4 p4 = *reinterpret_cast<const float4*>(pq);
+    const float4 v4 = *reinterpret_cast<const float4*>(vq);
+    if (kCheckV) {
+      vchk = __fmaf_rn(v4.x, 0.0f, vchk);
+      if (valid > 1) vchk = __fmaf_rn(v4.y, 0.0f, vchk);
+      if (valid > 2) vchk = __fmaf_rn(v4.z, 0.0f, vchk);
+      if (valid > 3) vchk = __fmaf_rn(v4.w, 0.0f, vchk);
+    }
+    uint4 w0, w1;
+    image(p4.x, v4.x, w0.x, w0.y);
+    image(p4.y, v4.y, w0.z, w0.w);
+    image(p4.z, v4.z, w1.x, w1.y);
+    image(p4.w, v4.w, w1.z, w1.w);
+    dst[0] = w0;
+    dst[C::kSlots] = w1;
+  };
   auto produce = [&](int t) {  // producers: the images of chunk t's products
     if (!active) return;
     const float* stage = raw + (t % C::kStages) * C::kRawWords;
-    const float* vt = stage + cc * C::kPitch;
-    const float* pr = stage + C::kComps * C::kPitch + h * C::kPitch;
-    double2* term = terms + (t & 1) * C::kTermStage + slot;
-    const int rows_here = min(C::kChunk, positions - t * C::kChunk);
     const int i0 = part * (4 * C::kPartQuads);
-    // A quad past rows_here reads stale words (the pitch covers it); the chains
-    // never add those terms.  Unrolled: the quads' loads issue together.
+    const float* vt = stage + cc * C::kPitch + i0;
+    const float* pr = stage + C::kComps * C::kPitch + h * C::kPitch + i0;
+    uint4* term = reinterpret_cast<uint4*>(terms) + (t & 1) * C::kTermStage + slot +
+                  (i0 >> 1) * C::kSlots;
+    const int rows_here = min(C::kChunk, positions - t * C::kChunk);
+    if (rows_here == C::kChunk) {
 #pragma unroll
-    for (int k = 0; k < C::kPartQuads; ++k) {
-      const int i = i0 + 4 * k;
-      if (i < rows_here) {
-        const float4 p4 = *reinterpret_cast<const float4*>(pr + i);
-        const float4 v4 = *reinterpret_cast<const float4*>(vt + i);
-        if (kCheckV) {
-          vchk = __fmaf_rn(v4.x, 0.0f, vchk);
-          if (i + 1 < rows_here) vchk = __fmaf_rn(v4.y, 0.0f, vchk);
-          if (i + 2 < rows_here) vchk = __fmaf_rn(v4.z, 0.0f, vchk);
-          if (i + 3 < rows_here) vchk = __fmaf_rn(v4.w, 0.0f, vchk);
-        }
-        term[(i >> 1) * C::kSlots] =
-            make_double2(scaled_image(__fmul_rn(p4.x, v4.x)), scaled_image(__fmul_rn(p4.y, v4.y)));
-        term[((i >> 1) + 1) * C::kSlots] =
-            make_double2(scaled_image(__fmul_rn(p4.z, v4.z)), scaled_image(__fmul_rn(p4.w, v4.w)));
-      }
+      for (int k = 0; k < C::kPartQuads; ++k)
+        quad(term + 2 * k * C::kSlots, pr + 4 * k, vt + 4 * k, 4);
+      return;
     }
+    // The last chunk: a quad past rows_here reads stale words (the pitch covers
+    // it); the chains never add those terms.
+    for (int k = 0; k < C::kPartQuads && i0 + 4 * k < rows_here; ++k)
+      quad(term + 2 * k * C::kSlots, pr + 4 * k, vt + 4 * k, rows_here - i0 - 4 * k);
   };
   double acc = 0.0;
   auto consume = [&](int t) {  // chain threads: chunk t's terms in position order
     const double2* term = terms + (t & 1) * C::kTermStage + slot;
     const int rows_here = min(C::kChunk, positions - t * C::kChunk);
-    const int pairs = rows_here >> 1;
-    int j = 0;
-    if (pairs >= 8) {
-      // the next four pairs load while the current four are added
-      double2 a[4];
+    if (rows_here == C::kChunk) {
+      // the next eight pairs load while the current eight are added
+      double2 a[8];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) a[k] = term[k * C::kSlots];
-      for (j = 4; j + 4 <= pairs; j += 4) {
-        double2 n[4];
+      for (int k = 0; k < 8; ++k) a[k] = term[k * C::kSlots];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) n[k] = term[(j + k) * C::kSlots];
+      for (int g = 1; g < C::kTermPairs / 8; ++g) {
+        double2 n[8];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 8; ++k) n[k] = term[(8 * g + k) * C::kSlots];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
           acc += a[k].x;
           acc += a[k].y;
           a[k] = n[k];
         }
       }
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < 8; ++k) {
         acc += a[k].x;
         acc += a[k].y;
       }
+      return;
     }
-    for (; j < pairs; ++j) {
+    const int pairs = rows_here >> 1;
+    for (int j = 0; j < pairs; ++j) {
       const double2 a = term[j * C::kSlots];
       acc += a.x;
       acc += a.y;
