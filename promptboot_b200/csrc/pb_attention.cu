@@ -29,7 +29,8 @@
 //    second chain adds integer-built f64 images of its products instead of
 //    converting them (scaled_product).
 //  * beyond that, the probabilities stay in the global scratch: the softmax
-//    launch and the one-chain-per-thread PV launch below.
+//    launch and the one-chain-per-thread PV launch below (up to 8 rows the
+//    chains are fed their f64 terms by producer warps, attention_pv_fed_kernel).
 #include "pb_common.cuh"
 #include "pb_kernels.cuh"
 #include "pb_quant.cuh"
